@@ -1,0 +1,404 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 token sampler on BASELINE.json's configurations.
+
+Default workload (config 4, the text decoder at Qwen3's vocabulary): bf16 logits [256, 151936],
+temperature 0.8, top-k 40, top-p 0.95, presence 0.5, frequency 0.3, 1024 history ids per row. The 256
+rows are sharded over the ranks as the config states (256/128/64/32 rows per GPU at 1/2/4/8 GPUs), so
+total work is fixed ("strong"); --scaling weak gives every rank 256 rows instead.
+
+A step = one pass of the sampler over one batch: one ssb_sample_rows call = one kernel launch. The
+launches are replayed from a CUDA graph over a pool of input batches whose total size exceeds twice the
+126 MB L2, so no step finds its logits in L2. `value` = rows sampled per second by all ranks, from CUDA
+events on the launching stream (max over ranks). `e2e` = the same through ssb_sample_host with pinned
+host buffers: the host->device copy of the step's inputs and the device->host copy of its ids inside
+the timed region. `cpu_baseline` = the reference's own sample() (compiled from its sources into
+oracle/_ref) on the box's host cores, on a bounded sample. --impl reference times that CPU sampler
+alone, with every host thread, on the same workload.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--config 1|2|3|4|5]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "speech.cpp_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+import numpy as np  # noqa: E402
+
+import speech_workloads as wl  # noqa: E402
+
+L2_BYTES = 126 * 1024 * 1024
+METRIC = "sampled rows/sec"
+UNIT = "rows/s"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["engine", "reference"], default="engine")
+    ap.add_argument("--config", type=int, default=4, choices=[1, 2, 3, 4, 5])
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong")
+    ap.add_argument("--rows", type=int, default=0, help="override the config's total rows")
+    ap.add_argument("--density", type=float, default=0.01, help="config 5 allow-mask density")
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------- workloads
+def workload(cfg: int, rows_total: int, rank: int, world: int, scaling: str, density: float):
+    """This rank's shard: dict(logits (f32 or uint16 bf16 bits), history, mask, mask_kind, u, params, desc)."""
+    import speech_sampler as ss
+    if cfg == 4:
+        total = rows_total or 256
+        n = total if scaling == "weak" else total // world
+        c = wl.config4(rows=n, row0=0 if scaling == "weak" else rank * n)
+        return dict(logits=c["logits_bf16"], history=c["history"], mask=None, mask_kind=ss.MASK_NONE, u=c["u"],
+                    params=c["params"], rows=n, total=n if scaling == "weak" else total,
+                    desc="config4 text decoder: bf16 [256, 151936], T 0.8, top-k 40, top-p 0.95, presence 0.5, "
+                         "frequency 0.3, 1024 Zipf history ids per row")
+    if cfg == 1:
+        n = rows_total or 1
+        c = wl.config1(rows=n)
+        return dict(logits=c["logits"], history=None, mask=c["mask"], mask_kind=ss.MASK_BAN, u=None,
+                    params=c["params"], rows=n, total=n,
+                    desc="config1 greedy + 64-id suppress mask: fp32 [1, 151936] per step (ASR text head)")
+    if cfg == 2:
+        c = wl.config2(steps=64)
+        return dict(logits=c["logits"][:1], history=c["history"][:1], mask=None, mask_kind=ss.MASK_NONE,
+                    u=c["u"][:1], params=c["params"], rows=1, total=1, pool=c,
+                    desc="config2 talker: fp32 [1, 3072], T 0.9, top-k 50, rep 1.05 over 512 ids, one row per step")
+    if cfg == 3:
+        c = wl.config3(steps=1)
+        return dict(logits=c["logits"][0], history=None, mask=None, mask_kind=ss.MASK_NONE, u=c["u"][0],
+                    params=c["params"], rows=64, total=64,
+                    desc="config3 code predictor: fp32 [64, 2048], T 0.9, top-k 50, 64 streams per step")
+    total = rows_total or 64
+    n = total // world
+    c = wl.config5(rows=n, density=density, row0=rank * n)
+    return dict(logits=c["logits"], history=None, mask=c["mask"], mask_kind=ss.MASK_ALLOW, u=c["u"], params=c["params"],
+                rows=n, total=total, desc=f"config5 constrained: fp32 [{total}, 151936], allow density {density}, "
+                                         "T 1, top-k 0, top-p 0.9")
+
+
+# ---------------------------------------------------------------- clocks during the timed region
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            return None
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() in ("active", "0x1") or val == "1":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- CPU legs
+def cpu_reference_time(w, rows_sample: int, threads: int):
+    """The reference's sample() over `rows_sample` rows (the shard's rows repeated), `threads` workers."""
+    from oracle import RefSampler, params as oparams
+    ref = RefSampler()
+    x = w["logits"]
+    x = wl.bf16_bits_to_f32(x) if x.dtype == np.uint16 else x
+    reps = int(math.ceil(rows_sample / x.shape[0]))
+    xs = np.tile(x, (reps, 1))[:rows_sample]
+    hs = None if w["history"] is None else np.tile(w["history"], (reps, 1))[:rows_sample]
+    us = None if w["u"] is None else np.tile(w["u"], reps)[:rows_sample]
+    banned = None
+    if w["mask"] is not None:
+        bits = np.unpackbits(w["mask"].view(np.uint8), axis=-1, bitorder="little")[..., :x.shape[1]].astype(bool)
+        banned = bits if w["mask_kind"] == 1 else ~bits
+        if banned.ndim == 2:
+            banned = np.tile(banned, (reps, 1))[:rows_sample]
+    secs, ids, status = ref.time_rows(xs, oparams(**w["params"]), hs, None, banned, us, threads)
+    return secs, ids, status
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_reference(args):
+    rank, _, world = dist_env()
+    if rank != 0:
+        return
+    w = workload(args.config, args.rows, 0, 1, "strong", args.density)
+    cores = host_cores()
+    rows = w["total"]
+    for _ in range(args.warmup):
+        cpu_reference_time(w, rows, cores)
+    t = 0.0
+    for _ in range(args.steps):
+        secs, _, status = cpu_reference_time(w, rows, cores)
+        t += secs
+    value = rows * args.steps / t
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * t / args.steps, "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
+            "dtype": "fp32 (bf16 rows widened; the reference takes fp32 only)", "data": "synthetic (seeded)",
+            "impl": "reference",
+            "config": {"workload": w["desc"], "rows_per_step": rows},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "reference",
+                             "sample": f"every step: the full {rows}-row batch through the reference's sample() "
+                                       f"(oracle/_ref, compiled from its sources), rows split over {cores} threads; "
+                                       "presence/frequency (not in the reference) applied to the row copy first"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- the engine
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    rank, local_rank, world = dist_env()
+    import torch
+    import torch.distributed as dist
+    import speech_sampler as ss
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local_rank))
+    w = workload(args.config, args.rows, rank, world, args.scaling, args.density)
+    sampler = ss.Sampler(local_rank)
+    p = ss.params(**w["params"])
+    bf16 = w["logits"].dtype == np.uint16
+    x_host = w["logits"]
+    rows, vocab = x_host.shape
+    batch_bytes = x_host.nbytes
+    pool_n = max(2, int(math.ceil(2 * L2_BYTES / batch_bytes)) + 1)
+    xt = torch.from_numpy(x_host)
+    xt = xt.view(torch.bfloat16) if bf16 else xt
+    pool = [xt.cuda() for _ in range(pool_n)]
+    hist = None if w["history"] is None else torch.from_numpy(w["history"]).cuda()
+    mask = None if w["mask"] is None else torch.from_numpy(w["mask"].view(np.int32)).cuda()
+    u = None if w["u"] is None else torch.from_numpy(w["u"]).cuda()
+    ids = [torch.empty(rows, dtype=torch.int32, device="cuda") for _ in range(pool_n)]
+    status = [torch.empty(rows, dtype=torch.int32, device="cuda") for _ in range(pool_n)]
+    stream = torch.cuda.Stream()
+
+    def launch(i, s):
+        sampler.sample(pool[i], p, hist, None, mask, w["mask_kind"], u, ids=ids[i], status=status[i], stream=s)
+
+    # correctness of the timed configuration against the oracle on a few rows (rank 0)
+    with torch.cuda.stream(stream):
+        for i in range(pool_n):
+            launch(i, stream)
+    stream.synchronize()
+    check = None
+    if rank == 0:
+        from oracle import Oracle, params as oparams
+        o = Oracle()
+        n_chk = min(rows, 8)
+        want, wst, _ = o.sample_rows(x_host[:n_chk], oparams(**w["params"]),
+                                     history=None if w["history"] is None else w["history"][:n_chk],
+                                     mask=None if w["mask"] is None else (w["mask"] if w["mask"].ndim == 1 else w["mask"][:n_chk]),
+                                     mask_kind=w["mask_kind"], u=None if w["u"] is None else w["u"][:n_chk])
+        got = ids[0][:n_chk].cpu().numpy()
+        check = bool(np.array_equal(got, want)) and all(bool(torch.equal(ids[0], t)) for t in ids[1:])
+        if not check:
+            print(json.dumps({"error": "engine ids differ from the oracle", "got": got.tolist(), "want": want.tolist()}),
+                  file=sys.stderr)
+
+    # capture one launch per pool batch into a CUDA graph
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        for i in range(pool_n):  # warm the stream before capture
+            launch(i, stream)
+    stream.synchronize()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(pool_n):
+            launch(i, torch.cuda.current_stream())
+    torch.cuda.synchronize()
+
+    def run_steps(k):
+        """k launches: whole graph replays plus single launches for the remainder."""
+        full, rest = divmod(k, pool_n)
+        with torch.cuda.stream(stream):
+            for _ in range(full):
+                graph.replay()
+            for i in range(rest):
+                launch(i, stream)
+
+    clocks = Clocks(local_rank)
+    clocks.start()
+    t_load = time.perf_counter()
+    run_steps(max(args.warmup, 3))
+    stream.synchronize()
+    # keep the GPU under load for ~1 s before the timed region so clock samples cover it
+    while time.perf_counter() - t_load < 1.0:
+        run_steps(pool_n * 16)
+        stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    run_steps(args.steps)
+    e1.record(stream)
+    stream.synchronize()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    ms_per_step = ms / args.steps
+    total_rows = w["total"] if args.scaling == "strong" else rows * world
+    value = total_rows / (ms_per_step * 1e-3)
+
+    # ---- end to end through the host-buffer entry point (pinned host memory)
+    pin_x = torch.empty(xt.shape, dtype=xt.dtype, pin_memory=True)
+    pin_x.copy_(xt)
+    px = pin_x.view(torch.int16).numpy().view(np.uint16) if bf16 else pin_x.numpy()
+    ph = None
+    if w["history"] is not None:
+        ph_t = torch.empty(w["history"].shape, dtype=torch.int32, pin_memory=True)
+        ph_t.copy_(torch.from_numpy(w["history"]))
+        ph = ph_t.numpy()
+    pu = None
+    if w["u"] is not None:
+        pu_t = torch.empty(w["u"].shape, dtype=torch.float64, pin_memory=True)
+        pu_t.copy_(torch.from_numpy(w["u"]))
+        pu = pu_t.numpy()
+    pm = w["mask"]
+    out_ids = torch.empty(rows, dtype=torch.int32, pin_memory=True).numpy()
+    out_st = torch.empty(rows, dtype=torch.int32, pin_memory=True).numpy()
+    sampler.reserve(rows, vocab)
+    for _ in range(3):
+        sampler.sample_host(px, p, ph, None, pm, w["mask_kind"], pu, ids=out_ids, status=out_st, stream=stream)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        sampler.sample_host(px, p, ph, None, pm, w["mask_kind"], pu, ids=out_ids, status=out_st, stream=stream)
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_value = total_rows * args.e2e_steps / e2e_s
+    h2d = px.nbytes + (0 if ph is None else ph.nbytes) + (0 if pu is None else pu.nbytes) + (0 if pm is None else pm.nbytes)
+    d2h = out_ids.nbytes + out_st.nbytes
+    e2e_ok = bool(np.array_equal(out_ids, ids[0].cpu().numpy()))
+
+    if rank == 0:
+        peak, peak_kind = peaks()
+        es = 2 if bf16 else 4
+        bytes_per_launch = rows * vocab * es
+        achieved = bytes_per_launch / (ms_per_step * 1e-3) / 1e9
+        traffic = None
+        tf = os.path.join(ROOT, "profiles", "traffic.json")
+        if os.path.exists(tf):
+            try:
+                tj = json.load(open(tf))
+                key = f"config{args.config}_rows{rows}"
+                traffic = tj.get(key)
+            except Exception:
+                traffic = None
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                cores = host_cores()
+                s1, _, _ = cpu_reference_time(w, min(rows, 64) if vocab > 10000 else 512, 1)
+                n1 = min(rows, 64) if vocab > 10000 else 512
+                n_all = min(max(rows, 8 * cores), 8192) if vocab > 10000 else 20000
+                sa, ids_ref, st_ref = cpu_reference_time(w, n_all, cores)
+                cpu = {"value": n_all / sa, "unit": UNIT, "cores": cores, "kind": "reference",
+                       "single_core_value": n1 / s1,
+                       "sample": f"{n_all} rows of this workload (the shard's rows repeated) through the reference's "
+                                 f"sample() compiled from its sources (oracle/_ref), split over {cores} std::threads; "
+                                 f"single core: {n1} rows. bf16 rows widened to fp32 untimed; presence/frequency "
+                                 "(absent from the reference) applied to each row copy inside the timed region"}
+            except Exception as ex:  # the reference library is absent
+                cpu = {"value": None, "unit": UNIT, "cores": 0, "kind": "reference", "sample": f"unavailable: {ex}"}
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
+            "dtype": "bf16" if bf16 else "f32", "data": "synthetic (seeded, host-generated; no dataset)",
+            "config": {"workload": w["desc"], "rows_per_gpu": rows, "rows_total": total_rows, "vocab": vocab,
+                       "l2": f"inputs larger than L2: a pool of {pool_n} input batches ({pool_n * batch_bytes / 2**20:.0f} MiB) "
+                             "cycled by CUDA-graph replay", "parallelism": f"batch-partitioned x{world}, no collective",
+                       "oracle_check_rows_equal": check},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": traffic, "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_launch": bytes_per_launch,
+                         "note": "logits bytes read per launch / average launch time (graph-replayed back to back)"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "steps": args.e2e_steps, "ids_equal_device_path": e2e_ok,
+                    "path": "ssb_sample_host: pinned host buffers, H2D + kernel + D2H + bounded wait per step"},
+            "gpu_launches": args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,170 @@
+/*
+ * speech_sampler_b200 — the C ABI of the B200 token-sampling and logit-processing engine.
+ *
+ * This is the boundary a speech.cpp build links against in place of its CPU sampler. Every call takes
+ * plain device pointers and sizes (no C++ or torch types), never throws, never falls back to the CPU,
+ * and reports failures as an ssb_status plus a thread-local message (ssb_last_error()). Per-row
+ * numerical refusals (the reference's exceptions) come back as ssb_row_status codes in `status[]`.
+ *
+ * Reference interfaces replaced (paths in the speech.cpp source tree):
+ *   sample(logits, SamplingParams, history, banned, u)  src/families/qwen3-tts/sampler.h:61-62, .cpp:103-111
+ *   sample(..., std::mt19937_64&)                       src/families/qwen3-tts/sampler.h:65-66, .cpp:113-116
+ *   candidates(logits, SamplingParams, history, banned) src/families/qwen3-tts/sampler.h:52-53, .cpp:69-101
+ *   GraphSampler::pick/draw/read (device picks)         src/families/qwen3-tts/graph-sampler.h:30-45
+ *   Qwen3Readback::Pick (device argmax, ASR greedy)     src/common/qwen3-decoder.h:80-92, .cpp:422-437
+ *   Qwen3Decoder verify() argmax over [n, vocab]        src/common/qwen3-decoder.cpp:492-510
+ *   host greedy max_element (ASR)                       src/families/qwen3-asr/decoder.cpp:108-113
+ *   Error(Fault, message, input) refusals               src/common/error.h:8-38
+ */
+#ifndef SPEECH_SAMPLER_B200_H
+#define SPEECH_SAMPLER_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define SSB_API __attribute__((visibility("default")))
+#else
+#define SSB_API
+#endif
+
+/* Call status. Mirrors the reference's Fault kinds (src/common/error.h:8-21) that this path can raise. */
+typedef enum ssb_status {
+    SSB_OK = 0,
+    SSB_INVALID_ARGUMENT = 1, /* Fault::InvalidArgument: a null pointer, a negative size, a bad enum */
+    SSB_OUT_OF_RANGE = 2,     /* Fault::OutOfRange: a size beyond an engine limit (message names it) */
+    SSB_DEVICE = 3,           /* Fault::Device: a CUDA error */
+    SSB_OUT_OF_MEMORY = 4     /* Fault::OutOfMemory: device scratch could not be allocated */
+} ssb_status;
+
+/*
+ * Per-row outcome, written to status[row]. The C++ host wrapper (speech_sampler_b200.hpp) turns each
+ * into the reference's exception:
+ *   PENALTY_OVERFLOW     -> Error(OutOfRange, ..., "repetition_penalty")   qwen3-tts/sampler.cpp:43-47
+ *   TEMPERATURE_OVERFLOW -> temperature_overflow(T), input "temperature"   sampling.cpp:21-25, sampler.cpp:82-83
+ *   NO_FINITE_LOGIT      -> std::runtime_error("no token has a finite logit to pick from")  sampler.cpp:49
+ *   NON_FINITE_INPUT     -> Error(Device, ...)  a NaN among the restricted logits (haru/sampler.cpp:21-23)
+ *   INVALID_ROW          -> a row whose own parameters exceed the launch's bounds (ssb_rows.max_top_k)
+ */
+typedef enum ssb_row_status {
+    SSB_ROW_OK = 0,
+    SSB_ROW_PENALTY_OVERFLOW = 1,
+    SSB_ROW_TEMPERATURE_OVERFLOW = 2,
+    SSB_ROW_NO_FINITE_LOGIT = 3,
+    SSB_ROW_NON_FINITE_INPUT = 4,
+    SSB_ROW_INVALID_ROW = 5
+} ssb_row_status;
+
+typedef enum ssb_dtype { SSB_F32 = 0, SSB_BF16 = 1 } ssb_dtype;
+
+/* BAN: a set bit removes the token (the reference's `banned`, qwen3-tts/sampler.cpp:40-42).
+ * ALLOW: a clear bit removes the token (extension: the complement of `banned`). */
+typedef enum ssb_mask_kind { SSB_MASK_NONE = 0, SSB_MASK_BAN = 1, SSB_MASK_ALLOW = 2 } ssb_mask_kind;
+
+/*
+ * Sampling settings of one row. The first five fields are the reference's SamplingParams
+ * (src/families/qwen3-tts/sampler.h:12-24) with the same meaning and defaults
+ * {greedy 0, temperature 1, top_k 0 (= every token), top_p 1, repetition_penalty 1}. The penalties
+ * after them are extensions (0 = off): for each distinct in-range history id with c occurrences,
+ * after the repetition penalty, l = l - frequency_penalty * c; l = l - presence_penalty (fp32).
+ */
+typedef struct ssb_params {
+    int32_t greedy;
+    float temperature;
+    int32_t top_k;
+    float top_p;
+    float repetition_penalty;
+    float presence_penalty;
+    float frequency_penalty;
+    int32_t reserved; /* must be 0 */
+} ssb_params;
+
+/*
+ * One batch of independent rows; every pointer is DEVICE memory unless it says otherwise.
+ * Row r's logits are logits + r*ld (dtype elements, ld >= vocab). Row r's mask words are
+ * mask + r*mask_ld (bit (t & 31) of word t >> 5 is token t; mask_ld 0 shares one mask by all rows).
+ * Row r's history is history + r*history_ld, of history_len[r] ids (or history_ld ids where
+ * history_len is NULL); ids outside [0, vocab) are skipped, as the reference skips them
+ * (qwen3-tts/sampler.cpp:35), so -1 padding is allowed.
+ * u[r] is the number uniform() drew for row r (sampling.cpp:5-7); greedy rows never read it.
+ * row_params (nullable) gives each row its own settings; the launch then needs max_top_k, the
+ * largest effective top-k of any drawing row (0 = some row keeps every token); a row beyond it gets
+ * SSB_ROW_INVALID_ROW. Without row_params, `params` applies to all rows and max_top_k is ignored.
+ */
+typedef struct ssb_rows {
+    const void *logits;
+    int64_t ld;
+    int32_t dtype; /* ssb_dtype */
+    int32_t rows;
+    int32_t vocab;
+    int32_t max_top_k;
+    ssb_params params;
+    const ssb_params *row_params;
+    const int32_t *history;
+    int64_t history_ld;
+    const int32_t *history_len;
+    const uint32_t *mask;
+    int64_t mask_ld;
+    int32_t mask_kind; /* ssb_mask_kind */
+    int32_t reserved;  /* must be 0 */
+    const double *u;
+    int32_t *ids;    /* out: the sampled token, -1 where status != OK */
+    int32_t *status; /* out: ssb_row_status */
+} ssb_rows;
+
+typedef struct ssb_context ssb_context;
+
+/* Engine limits (also reported in messages). */
+#define SSB_MAX_VOCAB 16777216      /* 2^24 tokens per row */
+#define SSB_MAX_STREAM_HISTORY 8192 /* history_ld limit for rows of more than SSB_SMALL_VOCAB tokens */
+#define SSB_SMALL_VOCAB 8192        /* rows up to this size are sampled whole from shared memory */
+
+/* Library version, "major.minor.patch". */
+SSB_API const char *ssb_version(void);
+
+/* The message of the last failing call on this thread ("" after a success). */
+SSB_API const char *ssb_last_error(void);
+
+/* A context on CUDA device `device`: owns the split-row scratch and the host-call staging buffers.
+ * One context per device and stream; calls on one context must not overlap in time. */
+SSB_API ssb_status ssb_context_create(int32_t device, ssb_context **out);
+SSB_API ssb_status ssb_context_destroy(ssb_context *ctx);
+
+/* Allocates scratch for batches up to max_rows rows of max_vocab tokens, so that later calls of that
+ * size allocate nothing (required before capturing them into a CUDA graph). */
+SSB_API ssb_status ssb_context_reserve(ssb_context *ctx, int32_t max_rows, int32_t max_vocab);
+
+/*
+ * Samples every row of `rows` on `stream` (a cudaStream_t; NULL = the legacy default stream):
+ * penalties -> mask -> temperature -> top-k -> softmax (double) -> top-p -> pick, or the first
+ * maximum for greedy rows, exactly as the reference's sample() (qwen3-tts/sampler.cpp:103-111) with
+ * ties broken by lowest token index. Asynchronous: ids/status are valid once the stream reaches them.
+ */
+SSB_API ssb_status ssb_sample_rows(ssb_context *ctx, const ssb_rows *rows, void *stream);
+
+/*
+ * The parity / debug export of candidates() (qwen3-tts/sampler.cpp:69-101): for each row, up to `cap`
+ * kept tokens in candidate order with their weights (normalized by the sum over the top-k, before
+ * the top-p cut, as the reference returns them) into tokens[row*cap ..], weights[row*cap ..], and
+ * the full kept count into count[row]. `processed` (nullable, f32 [rows, vocab]) receives the
+ * restricted logits: penalties and mask applied, before the temperature. Also writes ids/status.
+ */
+SSB_API ssb_status ssb_candidates_rows(ssb_context *ctx, const ssb_rows *rows, int32_t cap, int32_t *tokens,
+                                       double *weights, int32_t *count, float *processed, void *stream);
+
+/*
+ * sample() for HOST buffers, as the reference's call sites hold them (a logits readback, a history
+ * vector, a ban list): copies the inputs to context-owned device buffers, samples, copies ids and
+ * status back and waits for the stream. Pointers in `rows` are HOST pointers here.
+ */
+SSB_API ssb_status ssb_sample_host(ssb_context *ctx, const ssb_rows *rows, void *stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* SPEECH_SAMPLER_B200_H */

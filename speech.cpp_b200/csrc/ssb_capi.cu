@@ -1,0 +1,394 @@
+// The C ABI of include/speech_sampler_b200.h: argument checks, the choice of kernel, the context's
+// scratch, and the host-buffer entry point. No CPU sampling exists behind it: every row is sampled by
+// the CUDA kernels of ssb_small.cu / ssb_stream.cu, or the call fails.
+#include <algorithm>
+#include <chrono>
+#include <cstdint>
+#include <cstring>
+#include <string>
+#include <thread>
+
+#include <cuda_runtime.h>
+
+#include "speech_sampler_b200.h"
+#include "ssb_device.cuh"
+#include "ssb_kernels.h"
+
+struct ssb_context {
+    int device = 0;
+    int sm_count = 0;
+    int max_slots = 0;  // resident CTAs of the streaming kernel the scratch is sized for
+    // split-row scratch, sized once at creation (rows * splits never exceeds max_slots)
+    uint64_t * part_cand = nullptr;  // [max_slots * kStreamMaxK]
+    int32_t * part_n = nullptr;      // [max_slots]
+    float * part_max = nullptr;      // [max_slots]
+    int32_t * part_flags = nullptr;  // [max_slots]
+    uint32_t * counters = nullptr;   // [max_slots]
+    // host-call staging
+    unsigned char * stage = nullptr;
+    size_t stage_bytes = 0;
+    cudaEvent_t done = nullptr;
+    // occupancy of the streaming kernel per (mode, bf16, vec), measured at the row's full width
+    int occupancy[2][2][2] = {};
+};
+
+namespace {
+
+thread_local std::string g_error;
+
+ssb_status fail(ssb_status s, const std::string & message) {
+    g_error = message;
+    return s;
+}
+
+ssb_status ok() {
+    g_error.clear();
+    return SSB_OK;
+}
+
+ssb_status cuda_fail(cudaError_t e, const char * what) {
+    const ssb_status s = e == cudaErrorMemoryAllocation ? SSB_OUT_OF_MEMORY : SSB_DEVICE;
+    return fail(s, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// Makes the context's device current for the calling thread; restores nothing (CUDA convention).
+ssb_status use_device(const ssb_context * ctx) {
+    int cur = -1;
+    cudaError_t e = cudaGetDevice(&cur);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (cur != ctx->device) {
+        e = cudaSetDevice(ctx->device);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    }
+    return SSB_OK;
+}
+
+int64_t div_up(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+struct Plan {
+    int kernel;  // 0 small, 1 stream
+    int mode;    // stream: 0 greedy, 1 top-k
+    int k_bound;
+};
+
+ssb_status check_rows(const ssb_rows * r, bool device_side, Plan * plan) {
+    if (!r) return fail(SSB_INVALID_ARGUMENT, "rows is null");
+    if (r->rows < 0) return fail(SSB_INVALID_ARGUMENT, "rows is negative");
+    if (r->vocab < 1) return fail(SSB_INVALID_ARGUMENT, "vocab must be at least 1");
+    if (r->vocab > SSB_MAX_VOCAB) return fail(SSB_OUT_OF_RANGE, "vocab exceeds SSB_MAX_VOCAB (16777216)");
+    if (r->ld < r->vocab) return fail(SSB_INVALID_ARGUMENT, "ld is smaller than vocab");
+    if (r->dtype != SSB_F32 && r->dtype != SSB_BF16) return fail(SSB_INVALID_ARGUMENT, "dtype is neither SSB_F32 nor SSB_BF16");
+    if (r->mask_kind < SSB_MASK_NONE || r->mask_kind > SSB_MASK_ALLOW) return fail(SSB_INVALID_ARGUMENT, "mask_kind is not an ssb_mask_kind");
+    if (r->reserved != 0 || r->params.reserved != 0) return fail(SSB_INVALID_ARGUMENT, "reserved fields must be 0");
+    if (r->rows == 0) return SSB_OK;
+    if (!r->logits) return fail(SSB_INVALID_ARGUMENT, "logits is null");
+    if (!r->ids || !r->status) return fail(SSB_INVALID_ARGUMENT, "ids and status are required");
+    if (r->mask_kind != SSB_MASK_NONE) {
+        if (!r->mask) return fail(SSB_INVALID_ARGUMENT, "mask_kind is set but mask is null");
+        if (r->mask_ld < 0) return fail(SSB_INVALID_ARGUMENT, "mask_ld is negative");
+        if (r->mask_ld > 0 && r->mask_ld < div_up(r->vocab, 32)) return fail(SSB_INVALID_ARGUMENT, "mask_ld is smaller than ceil(vocab / 32)");
+    }
+    if (r->history) {
+        if (r->history_ld < 0) return fail(SSB_INVALID_ARGUMENT, "history_ld is negative");
+        if (r->history_ld > INT32_MAX / 2) return fail(SSB_OUT_OF_RANGE, "history_ld is too large");
+    }
+    const bool all_greedy = !r->row_params && r->params.greedy;
+    if (!all_greedy && !r->u) return fail(SSB_INVALID_ARGUMENT, "u is required where a row draws (not greedy)");
+    int kb;
+    if (r->row_params) {
+        if (r->max_top_k < 0) return fail(SSB_INVALID_ARGUMENT, "max_top_k is negative");
+        kb = r->max_top_k > 0 ? std::min(r->max_top_k, r->vocab) : r->vocab;
+    } else {
+        kb = r->params.greedy ? 1 : (r->params.top_k > 0 ? std::min(r->params.top_k, r->vocab) : r->vocab);
+    }
+    plan->k_bound = kb;
+    if (r->vocab <= SSB_SMALL_VOCAB) {
+        plan->kernel = 0;
+        plan->mode = 0;
+        return SSB_OK;
+    }
+    if (r->history && r->history_ld > SSB_MAX_STREAM_HISTORY)
+        return fail(SSB_OUT_OF_RANGE, "history_ld exceeds SSB_MAX_STREAM_HISTORY (8192) for a vocabulary of more than 8192 tokens");
+    plan->kernel = 1;
+    plan->mode = all_greedy ? 0 : 1;
+    if (plan->mode == 1 && kb > ssb::kStreamMaxK)
+        return fail(SSB_OUT_OF_RANGE, "a top-k above 1024 (or 0 = every token) over a vocabulary of more than 8192 tokens "
+                                      "is not supported by this build");
+    (void) device_side;
+    return SSB_OK;
+}
+
+struct Debug {
+    int cap = 0;
+    int32_t * tokens = nullptr;
+    double * weights = nullptr;
+    int32_t * count = nullptr;
+    float * processed = nullptr;
+};
+
+ssb::RowsArgs rows_args(const ssb_rows * r, int k_bound, const Debug * dbg) {
+    ssb::RowsArgs a{};
+    a.logits = r->logits;
+    a.ld = r->ld;
+    a.rows = r->rows;
+    a.vocab = r->vocab;
+    a.params = r->params;
+    a.row_params = r->row_params;
+    a.k_bound = k_bound;
+    a.history = r->history;
+    a.history_ld = r->history ? r->history_ld : 0;
+    a.history_len = r->history ? r->history_len : nullptr;
+    a.mask = r->mask_kind != SSB_MASK_NONE ? r->mask : nullptr;
+    a.mask_ld = r->mask_ld;
+    a.mask_kind = r->mask_kind;
+    a.u = r->u;
+    a.ids = r->ids;
+    a.status = r->status;
+    if (dbg) {
+        a.dbg_cap = dbg->cap;
+        a.dbg_tokens = dbg->tokens;
+        a.dbg_weights = dbg->weights;
+        a.dbg_count = dbg->count;
+        a.dbg_processed = dbg->processed;
+    }
+    return a;
+}
+
+ssb_status run(ssb_context * ctx, const ssb_rows * r, const Debug * dbg, cudaStream_t stream) {
+    Plan plan{};
+    ssb_status s = check_rows(r, true, &plan);
+    if (s != SSB_OK) return s;
+    if (!ctx) return fail(SSB_INVALID_ARGUMENT, "ctx is null");
+    if (r->rows == 0) return ok();
+    s = use_device(ctx);
+    if (s != SSB_OK) return s;
+    const bool bf16 = r->dtype == SSB_BF16;
+    const bool debug = dbg != nullptr;
+    ssb::RowsArgs a = rows_args(r, plan.k_bound, dbg);
+    cudaError_t e;
+    if (plan.kernel == 0) {
+        e = ssb::launch_small(a, bf16, debug, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "small-row kernel launch");
+        return ok();
+    }
+    const int mode = plan.mode;
+    const int es = bf16 ? 2 : 4;
+    const bool vec = (reinterpret_cast<uintptr_t>(r->logits) % 16 == 0) && ((r->ld * es) % 16 == 0);
+    const int g = vec ? 16 / es : 1;
+    const int kb = std::max(1, plan.k_bound);
+    a.k_bound = kb;
+    ssb::StreamArgs sa{};
+    sa.r = a;
+    sa.hist_slots = r->history ? ssb::next_pow2((int) std::max<int64_t>(2, r->history_ld)) : 0;
+    sa.cap = mode == 1 ? (int) div_up(ssb::kStreamThreads * g + kb + std::max(1024, kb), 32) * 32 : 0;
+    sa.sel_slots = mode == 1 ? ssb::next_pow2(std::max(kb, 2)) : 0;
+    int & occ = ctx->occupancy[mode][bf16][vec];
+    if (occ == 0) {
+        const int full_chunk = (int) div_up(r->vocab, 32) * 32;
+        occ = ssb::stream_blocks_per_sm(mode, bf16, vec, ssb::stream_smem_bytes(mode, full_chunk, sa.hist_slots, sa.cap, sa.sel_slots));
+        if (occ <= 0) return fail(SSB_DEVICE, "the streaming kernel does not fit on this device");
+    }
+    const int slots = std::min(ctx->max_slots, ctx->sm_count * occ);
+    const int min_chunk = mode == 0 ? 2048 : 4096;
+    int64_t splits = std::max<int64_t>(1, std::min<int64_t>(div_up(r->vocab, min_chunk), slots / std::max(1, r->rows)));
+    int64_t chunk = div_up(div_up(r->vocab, splits), 32) * 32;
+    splits = div_up(r->vocab, chunk);
+    sa.splits = (int) splits;
+    sa.chunk = (int) chunk;
+    if (splits > 1) {
+        if ((int64_t) r->rows * splits > ctx->max_slots) return fail(SSB_OUT_OF_RANGE, "split-row scratch exceeded");
+        sa.part_cand = ctx->part_cand;
+        sa.part_n = ctx->part_n;
+        sa.part_max = ctx->part_max;
+        sa.part_flags = ctx->part_flags;
+        sa.counters = ctx->counters;
+    }
+    if ((int64_t) r->rows * splits > INT32_MAX) return fail(SSB_OUT_OF_RANGE, "too many rows for one launch");
+    e = ssb::launch_stream(sa, mode, bf16, vec, debug, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "streaming kernel launch");
+    return ok();
+}
+
+// Waits for `stream` with a bound; a device that stops answering becomes SSB_DEVICE, not a hang.
+ssb_status wait_stream(ssb_context * ctx, cudaStream_t stream, double timeout_s) {
+    cudaError_t e = cudaEventRecord(ctx->done, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+    const auto t0 = std::chrono::steady_clock::now();
+    for (long spin = 0;; spin++) {
+        e = cudaEventQuery(ctx->done);
+        if (e == cudaSuccess) return SSB_OK;
+        if (e != cudaErrorNotReady) return cuda_fail(e, "waiting for the sampler");
+        if (spin > 1000) {
+            std::this_thread::sleep_for(std::chrono::microseconds(20));
+            if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > timeout_s)
+                return fail(SSB_DEVICE, "the device did not finish sampling within the time limit");
+        }
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+const char * ssb_version(void) { return "0.1.0"; }
+
+const char * ssb_last_error(void) { return g_error.c_str(); }
+
+ssb_status ssb_context_create(int32_t device, ssb_context ** out) {
+    if (!out) return fail(SSB_INVALID_ARGUMENT, "out is null");
+    *out = nullptr;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+    if (device < 0 || device >= n) return fail(SSB_INVALID_ARGUMENT, "no CUDA device " + std::to_string(device));
+    auto * ctx = new ssb_context();
+    ctx->device = device;
+    ssb_status s = use_device(ctx);
+    if (s != SSB_OK) {
+        delete ctx;
+        return s;
+    }
+    e = cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device);
+    if (e != cudaSuccess) {
+        delete ctx;
+        return cuda_fail(e, "cudaDeviceGetAttribute");
+    }
+    ctx->max_slots = ctx->sm_count * 8;  // 8 CTAs of 256 threads fill an SM's 2048 threads
+    const size_t ms = (size_t) ctx->max_slots;
+    e = cudaMalloc(&ctx->part_cand, ms * ssb::kStreamMaxK * sizeof(uint64_t));
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->part_n, ms * sizeof(int32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->part_max, ms * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->part_flags, ms * sizeof(int32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->counters, ms * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(ctx->counters, 0, ms * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->done, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        ssb_context_destroy(ctx);
+        return cuda_fail(e, "context scratch");
+    }
+    *out = ctx;
+    return ok();
+}
+
+ssb_status ssb_context_destroy(ssb_context * ctx) {
+    if (!ctx) return ok();
+    int cur = -1;
+    cudaGetDevice(&cur);
+    cudaSetDevice(ctx->device);
+    cudaFree(ctx->part_cand);
+    cudaFree(ctx->part_n);
+    cudaFree(ctx->part_max);
+    cudaFree(ctx->part_flags);
+    cudaFree(ctx->counters);
+    cudaFree(ctx->stage);
+    if (ctx->done) cudaEventDestroy(ctx->done);
+    if (cur >= 0) cudaSetDevice(cur);
+    delete ctx;
+    return ok();
+}
+
+ssb_status ssb_context_reserve(ssb_context * ctx, int32_t max_rows, int32_t max_vocab) {
+    if (!ctx) return fail(SSB_INVALID_ARGUMENT, "ctx is null");
+    if (max_rows < 0 || max_vocab < 0) return fail(SSB_INVALID_ARGUMENT, "negative size");
+    // Split-row scratch is allocated at creation; reserving sizes the host-call staging buffer for
+    // f32 rows, histories of up to SSB_MAX_STREAM_HISTORY ids and per-row masks.
+    ssb_status s = use_device(ctx);
+    if (s != SSB_OK) return s;
+    const size_t rows = (size_t) max_rows, vocab = (size_t) max_vocab;
+    const size_t need = rows * vocab * 4 + rows * SSB_MAX_STREAM_HISTORY * 4 + rows * ((vocab + 31) / 32) * 4 +
+                        rows * (8 + 4 + 4 + 4 + sizeof(ssb_params)) + 8 * 256;
+    if (need > ctx->stage_bytes) {
+        cudaFree(ctx->stage);
+        ctx->stage = nullptr;
+        ctx->stage_bytes = 0;
+        cudaError_t e = cudaMalloc(&ctx->stage, need);
+        if (e != cudaSuccess) return cuda_fail(e, "staging buffer");
+        ctx->stage_bytes = need;
+    }
+    return ok();
+}
+
+ssb_status ssb_sample_rows(ssb_context * ctx, const ssb_rows * rows, void * stream) {
+    return run(ctx, rows, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+ssb_status ssb_candidates_rows(ssb_context * ctx, const ssb_rows * rows, int32_t cap, int32_t * tokens, double * weights,
+                               int32_t * count, float * processed, void * stream) {
+    if (cap < 0) return fail(SSB_INVALID_ARGUMENT, "cap is negative");
+    if (cap > 0 && (!tokens || !weights)) return fail(SSB_INVALID_ARGUMENT, "tokens and weights are required when cap > 0");
+    if (!count) return fail(SSB_INVALID_ARGUMENT, "count is required");
+    Debug dbg;
+    dbg.cap = cap;
+    dbg.tokens = cap > 0 ? tokens : nullptr;
+    dbg.weights = cap > 0 ? weights : nullptr;
+    dbg.count = count;
+    dbg.processed = processed;
+    return run(ctx, rows, &dbg, static_cast<cudaStream_t>(stream));
+}
+
+ssb_status ssb_sample_host(ssb_context * ctx, const ssb_rows * rows, void * stream_ptr) {
+    Plan plan{};
+    ssb_status s = check_rows(rows, false, &plan);
+    if (s != SSB_OK) return s;
+    if (!ctx) return fail(SSB_INVALID_ARGUMENT, "ctx is null");
+    if (rows->rows == 0) return ok();
+    s = use_device(ctx);
+    if (s != SSB_OK) return s;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    const ssb_rows & h = *rows;
+    const size_t n = (size_t) h.rows;
+    const size_t es = h.dtype == SSB_BF16 ? 2 : 4;
+    const size_t logit_bytes = ((n - 1) * (size_t) h.ld + (size_t) h.vocab) * es;
+    const size_t hist_bytes = h.history ? n * (size_t) h.history_ld * 4 : 0;
+    const size_t hlen_bytes = h.history && h.history_len ? n * 4 : 0;
+    const size_t mask_words = h.mask_kind != SSB_MASK_NONE ? (h.mask_ld ? n * (size_t) h.mask_ld : (size_t) div_up(h.vocab, 32)) : 0;
+    const size_t u_bytes = h.u ? n * 8 : 0;
+    const size_t rp_bytes = h.row_params ? n * sizeof(ssb_params) : 0;
+    auto al = [](size_t b) { return (b + 255) & ~(size_t) 255; };
+    const size_t need = al(logit_bytes) + al(hist_bytes) + al(hlen_bytes) + al(mask_words * 4) + al(u_bytes) + al(rp_bytes) +
+                        al(n * 4) * 2;
+    if (need > ctx->stage_bytes) {
+        cudaError_t e = cudaStreamSynchronize(stream);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+        cudaFree(ctx->stage);
+        ctx->stage = nullptr;
+        ctx->stage_bytes = 0;
+        e = cudaMalloc(&ctx->stage, need);
+        if (e != cudaSuccess) return cuda_fail(e, "staging buffer");
+        ctx->stage_bytes = need;
+    }
+    unsigned char * p = ctx->stage;
+    auto take = [&](size_t b) {
+        unsigned char * q = p;
+        p += al(b);
+        return q;
+    };
+    ssb_rows d = h;
+    cudaError_t e = cudaSuccess;
+    auto up = [&](const void * src, size_t bytes) -> void * {
+        if (!src || bytes == 0) return nullptr;
+        void * dst = take(bytes);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, stream);
+        return dst;
+    };
+    d.logits = up(h.logits, logit_bytes);
+    d.history = static_cast<const int32_t *>(up(h.history, hist_bytes));
+    d.history_len = static_cast<const int32_t *>(up(h.history ? h.history_len : nullptr, hlen_bytes));
+    d.mask = static_cast<const uint32_t *>(up(h.mask_kind != SSB_MASK_NONE ? h.mask : nullptr, mask_words * 4));
+    d.u = static_cast<const double *>(up(h.u, u_bytes));
+    d.row_params = static_cast<const ssb_params *>(up(h.row_params, rp_bytes));
+    d.ids = reinterpret_cast<int32_t *>(take(n * 4));
+    d.status = reinterpret_cast<int32_t *>(take(n * 4));
+    if (e != cudaSuccess) return cuda_fail(e, "copying the inputs to the device");
+    s = run(ctx, &d, nullptr, stream);
+    if (s != SSB_OK) return s;
+    e = cudaMemcpyAsync(h.ids, d.ids, n * 4, cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(h.status, d.status, n * 4, cudaMemcpyDeviceToHost, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "copying the ids back");
+    s = wait_stream(ctx, stream, 60.0);
+    if (s != SSB_OK) return s;
+    return ok();
+}
+
+}  // extern "C"

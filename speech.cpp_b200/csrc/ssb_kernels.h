@@ -1,0 +1,68 @@
+// Launch arguments of the sampler kernels (host <-> device, by value).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "speech_sampler_b200.h"
+
+namespace ssb {
+
+// Fields every kernel reads: the batch (device pointers) plus the optional parity/debug outputs.
+struct RowsArgs {
+    const void * logits;
+    int64_t ld;
+    int rows;
+    int vocab;
+    ssb_params params;
+    const ssb_params * row_params;
+    int k_bound;  // largest effective top-k of a drawing row (rows beyond it are INVALID_ROW)
+    const int32_t * history;
+    int64_t history_ld;
+    const int32_t * history_len;
+    const uint32_t * mask;
+    int64_t mask_ld;
+    int mask_kind;
+    const double * u;
+    int32_t * ids;
+    int32_t * status;
+    // debug / parity export (ssb_candidates_rows); null in the product path
+    int dbg_cap;
+    int32_t * dbg_tokens;
+    double * dbg_weights;
+    int32_t * dbg_count;
+    float * dbg_processed;
+};
+
+using SmallArgs = RowsArgs;
+
+// Split-row streaming kernels: `splits` CTAs per row, each streaming `chunk` columns; with more than
+// one split, each CTA leaves its partial result in the part_* scratch and the last CTA of the row
+// (by the per-row arrival counter) merges them. Counters return to 0 after every launch.
+struct StreamArgs {
+    RowsArgs r;
+    int splits;
+    int chunk;       // columns per split, a multiple of 32
+    int cap;         // candidate buffer entries per CTA (top-k mode)
+    int hist_slots;  // shared slots for in-range history ids (power of two >= history_ld)
+    int sel_slots;   // shared slots for the selected candidates (>= k_bound)
+    uint64_t * part_cand;  // [rows * splits * k_bound] composites
+    int32_t * part_n;      // [rows * splits]
+    float * part_max;      // [rows * splits] restricted maximum (NaN-propagating)
+    int32_t * part_flags;  // [rows * splits] bit 0: a scaled logit was NaN
+    uint32_t * counters;   // [rows]
+};
+
+constexpr int kStreamThreads = 256;
+constexpr int kStreamMaxK = 1024;  // largest top-k of the streaming path
+
+size_t small_smem_bytes(int vocab, int k_bound);
+cudaError_t launch_small(const SmallArgs & a, bool bf16, bool debug, cudaStream_t stream);
+
+// mode 0: every row greedy (argmax); mode 1: top-k draw (greedy rows as top-1 of unscaled logits)
+size_t stream_smem_bytes(int mode, int chunk, int hist_slots, int cap, int sel_slots);
+cudaError_t launch_stream(const StreamArgs & a, int mode, bool bf16, bool vec, bool debug, cudaStream_t stream);
+int stream_blocks_per_sm(int mode, bool bf16, bool vec, size_t smem);
+
+}  // namespace ssb

@@ -1,0 +1,179 @@
+// Small-vocabulary rows (vocab <= SSB_SMALL_VOCAB): one CTA samples one row entirely from shared
+// memory. This is the path of the Qwen3-TTS talker (3072 codes) and code predictor (2048 codes).
+//
+// Per row, in the reference's order (src/families/qwen3-tts/sampler.cpp):
+//   1. load the row into shared memory as fp32 (bf16 widened exactly);
+//   2. repetition penalty once per distinct in-range history id (:33-39; a shared count table plays the
+//      reference's `seen` bitmap), then the presence/frequency extension;
+//   3. ban/allow mask -> -inf (:40-42);
+//   4. max -> PENALTY_OVERFLOW / NO_FINITE_LOGIT (:43-49), NaN -> NON_FINITE_INPUT;
+//   5. greedy: first maximum (:105-108); else scale by the temperature (:73), top-k by radix select on
+//      composite keys, sort the k, softmax in double, top-p, pick (:76-99, sampling.cpp:9-19).
+#include "ssb_device.cuh"
+#include "ssb_kernels.h"
+
+namespace ssb {
+
+namespace {
+
+constexpr int kSmallThreads = 512;
+
+template <typename TIn, bool kDebug>
+__global__ void __launch_bounds__(kSmallThreads) small_rows_kernel(const SmallArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ SelectState sel;
+    __shared__ float s_redf[32];
+    __shared__ uint64_t s_red64[32];
+    __shared__ int s_redi[32];
+
+    const int row = blockIdx.x;
+    const int vocab = a.vocab;
+    const ssb_params pp = a.row_params ? a.row_params[row] : a.params;
+    const RowParams p = resolve_params(pp, vocab);
+    int32_t * id_out = a.ids + row;
+    int32_t * status_out = a.status + row;
+    RowOut out{id_out, status_out, nullptr, nullptr, nullptr, 0};
+    if (kDebug) {
+        out.tokens = a.dbg_tokens ? a.dbg_tokens + (int64_t) row * a.dbg_cap : nullptr;
+        out.weights = a.dbg_weights ? a.dbg_weights + (int64_t) row * a.dbg_cap : nullptr;
+        out.count = a.dbg_count ? a.dbg_count + row : nullptr;
+        out.cap = a.dbg_cap;
+    }
+    if (a.row_params && !p.greedy && p.k > a.k_bound) {
+        if (threadIdx.x == 0) *id_out = -1, *status_out = SSB_ROW_INVALID_ROW;
+        if (kDebug && out.count && threadIdx.x == 0) *out.count = 0;
+        return;
+    }
+
+    float * s_val = reinterpret_cast<float *>(smem);                       // [vocab]
+    unsigned char * s_after = smem + (((size_t) vocab * 4 + 15) & ~(size_t) 15);
+    uint32_t * s_cnt = reinterpret_cast<uint32_t *>(s_after);               // [vocab], aliased below
+
+    const TIn * src = reinterpret_cast<const TIn *>(a.logits) + (int64_t) row * a.ld;
+    for (int i = threadIdx.x; i < vocab; i += blockDim.x) s_val[i] = Elem<TIn>::load1(src, i);
+
+    // ---- penalties over the history
+    const int32_t * hist = a.history ? a.history + (int64_t) row * a.history_ld : nullptr;
+    int hlen = 0;
+    if (hist) {
+        hlen = a.history_len ? a.history_len[row] : (int) a.history_ld;
+        hlen = hlen < 0 ? 0 : (hlen > (int) a.history_ld ? (int) a.history_ld : hlen);
+    }
+    const bool penal = p.history_applies && hlen > 0;
+    if (penal) {
+        for (int i = threadIdx.x; i < vocab; i += blockDim.x) s_cnt[i] = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < hlen; i += blockDim.x) {
+            const int32_t t = hist[i];
+            if (t >= 0 && t < vocab) atomicAdd(&s_cnt[t], 1u);
+        }
+    }
+    __syncthreads();
+
+    // ---- penalties, mask, processed output, row statistics
+    const uint32_t * mrow = (a.mask && a.mask_kind != SSB_MASK_NONE) ? a.mask + (int64_t) row * a.mask_ld : nullptr;
+    float raw_max = -kInf;
+    uint64_t best = 0;  // greedy: composite of the unscaled value (first maximum = lowest index on ties)
+    for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+        float v = s_val[i];
+        if (penal) {
+            const uint32_t c = s_cnt[i];
+            if (c) v = penalize(v, (int) c, p);
+        }
+        if (mrow && masked_bit(mrow[i >> 5] >> (i & 31), a.mask_kind)) v = -kInf;
+        s_val[i] = v;
+        if (kDebug && a.dbg_processed) a.dbg_processed[(int64_t) row * vocab + i] = v;
+        raw_max = max_nan(raw_max, v);
+        const uint64_t c = composite(v, (uint32_t) i);
+        best = c > best ? c : best;
+    }
+    raw_max = block_max_nan(raw_max, s_redf);
+    const int st = restricted_status(raw_max, p.rep);
+    if (st != SSB_ROW_OK) {
+        if (threadIdx.x == 0) {
+            *id_out = -1, *status_out = st;
+            if (out.count) *out.count = 0;
+        }
+        return;
+    }
+    if (p.greedy) {
+        best = block_max_u64(best, s_red64);
+        if (threadIdx.x == 0) {
+            *id_out = (int32_t) composite_index(best), *status_out = SSB_ROW_OK;
+            if (out.count) *out.count = 1;
+            if (out.tokens && out.cap > 0) out.tokens[0] = *id_out, out.weights[0] = 1.0;
+        }
+        return;
+    }
+
+    // ---- temperature (qwen3-tts/sampler.cpp:73): every logit, including -inf, divided in fp32
+    int nan_scaled = 0;
+    for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+        const float s = __fdiv_rn(s_val[i], p.temperature);
+        nan_scaled |= s != s;
+        s_val[i] = s;
+    }
+    nan_scaled = block_or(nan_scaled, s_redi);
+    if (nan_scaled) {
+        if (threadIdx.x == 0) {
+            *id_out = -1, *status_out = SSB_ROW_TEMPERATURE_OVERFLOW;
+            if (out.count) *out.count = 0;
+        }
+        return;
+    }
+
+    // ---- top-k by radix select, then sort the k (s_cnt's space is reused for the candidates)
+    const int k = p.k;
+    radix_select(vocab, k, [&](int i) { return composite(s_val[i], (uint32_t) i); }, sel);
+    const int kp2 = next_pow2(k);
+    uint64_t * s_cand = reinterpret_cast<uint64_t *>(s_after);      // [kp2]
+    double * s_w = reinterpret_cast<double *>(s_cand + kp2);         // [k]
+    __shared__ int s_n;
+    if (threadIdx.x == 0) s_n = 0;
+    for (int i = kp2 - 1 - threadIdx.x; i >= k; i -= blockDim.x) s_cand[i] = 0;
+    __syncthreads();
+    for (int base = 0; base < vocab; base += blockDim.x) {
+        const int i = base + threadIdx.x;
+        const uint64_t c = i < vocab ? composite(s_val[i], (uint32_t) i) : 0;
+        const bool take = i < vocab && selected(c, sel);
+        const unsigned m = __ballot_sync(0xffffffffu, take);
+        if (m) {
+            int slot = 0;
+            if (lane_id() == __ffs(m) - 1) slot = atomicAdd(&s_n, __popc(m));
+            slot = __shfl_sync(0xffffffffu, slot, __ffs(m) - 1);
+            const int at = slot + __popc(m & ((1u << lane_id()) - 1));
+            if (take && at < kp2) s_cand[at] = c;
+        }
+    }
+    __syncthreads();
+    bitonic_sort_desc(s_cand, kp2);
+    const double u = a.u ? a.u[row] : 0.0;
+    finalize_draw(s_cand, k, p, u, s_w, out);
+}
+
+template <typename TIn, bool kDebug>
+cudaError_t launch_small_t(const SmallArgs & a, size_t smem, cudaStream_t stream) {
+    auto kern = small_rows_kernel<TIn, kDebug>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    if (e != cudaSuccess) return e;
+    kern<<<a.rows, kSmallThreads, smem, stream>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t small_smem_bytes(int vocab, int k_bound) {
+    const size_t vals = ((size_t) vocab * 4 + 15) & ~(size_t) 15;
+    const int kp2 = next_pow2(k_bound < 1 ? 1 : k_bound);
+    const size_t cnt = (size_t) vocab * 4;
+    const size_t cand = (size_t) kp2 * 8 + (size_t) k_bound * 8;
+    return vals + (cnt > cand ? cnt : cand);
+}
+
+cudaError_t launch_small(const SmallArgs & a, bool bf16, bool debug, cudaStream_t stream) {
+    const size_t smem = small_smem_bytes(a.vocab, a.k_bound);
+    if (bf16) return debug ? launch_small_t<uint16_t, true>(a, smem, stream) : launch_small_t<uint16_t, false>(a, smem, stream);
+    return debug ? launch_small_t<float, true>(a, smem, stream) : launch_small_t<float, false>(a, smem, stream);
+}
+
+}  // namespace ssb

@@ -1,0 +1,234 @@
+"""Python binding of libspeech_sampler_b200.so (the C ABI of include/speech_sampler_b200.h).
+
+A thin ctypes layer: it passes raw device pointers (from torch tensors, which serve only as device
+memory and streams here) or host pointers (numpy) to the CUDA engine, and raises on failure. There
+is no CPU fallback: if the library is missing or no GPU is present, construction fails.
+
+    s = Sampler(device=0)
+    ids, status = s.sample(logits, params(temperature=0.9, top_k=50), history=h, u=u)
+
+The settings mirror the reference's SamplingParams (src/families/qwen3-tts/sampler.h:12-24) plus the
+presence/frequency extensions; per-row statuses mirror its refusals (ROW_* below).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import numpy as np
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG)
+LIB_PATH = os.path.join(PKG, "libspeech_sampler_b200.so")
+HEADER = os.path.join(ROOT, "include", "speech_sampler_b200.h")
+
+OK, INVALID_ARGUMENT, OUT_OF_RANGE, DEVICE, OUT_OF_MEMORY = range(5)
+ROW_OK, ROW_PENALTY_OVERFLOW, ROW_TEMPERATURE_OVERFLOW, ROW_NO_FINITE_LOGIT, ROW_NON_FINITE_INPUT, ROW_INVALID_ROW = range(6)
+F32, BF16 = 0, 1
+MASK_NONE, MASK_BAN, MASK_ALLOW = 0, 1, 2
+SMALL_VOCAB = 8192
+MAX_STREAM_HISTORY = 8192
+STREAM_MAX_K = 1024
+
+
+class SsbError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"ssb status {status}: {message}")
+        self.status = status
+        self.message = message
+
+
+class Params(ctypes.Structure):
+    _fields_ = [("greedy", ctypes.c_int32), ("temperature", ctypes.c_float), ("top_k", ctypes.c_int32),
+                ("top_p", ctypes.c_float), ("repetition_penalty", ctypes.c_float),
+                ("presence_penalty", ctypes.c_float), ("frequency_penalty", ctypes.c_float),
+                ("reserved", ctypes.c_int32)]
+
+
+def params(greedy=False, temperature=1.0, top_k=0, top_p=1.0, repetition_penalty=1.0, presence_penalty=0.0,
+           frequency_penalty=0.0) -> Params:
+    """The reference's SamplingParams defaults (qwen3-tts/sampler.h:12-24) plus the extensions."""
+    return Params(int(bool(greedy)), temperature, int(top_k), top_p, repetition_penalty, presence_penalty,
+                  frequency_penalty, 0)
+
+
+PARAMS_DTYPE = np.dtype([("greedy", "<i4"), ("temperature", "<f4"), ("top_k", "<i4"), ("top_p", "<f4"),
+                         ("repetition_penalty", "<f4"), ("presence_penalty", "<f4"),
+                         ("frequency_penalty", "<f4"), ("reserved", "<i4")])
+
+
+def params_array(plist) -> np.ndarray:
+    """A [rows] structured array of ssb_params (for row_params)."""
+    a = np.zeros(len(plist), PARAMS_DTYPE)
+    for i, p in enumerate(plist):
+        a[i] = (p.greedy, p.temperature, p.top_k, p.top_p, p.repetition_penalty, p.presence_penalty,
+                p.frequency_penalty, 0)
+    return a
+
+
+class Rows(ctypes.Structure):
+    _fields_ = [("logits", ctypes.c_void_p), ("ld", ctypes.c_int64), ("dtype", ctypes.c_int32),
+                ("rows", ctypes.c_int32), ("vocab", ctypes.c_int32), ("max_top_k", ctypes.c_int32),
+                ("params", Params), ("row_params", ctypes.c_void_p), ("history", ctypes.c_void_p),
+                ("history_ld", ctypes.c_int64), ("history_len", ctypes.c_void_p), ("mask", ctypes.c_void_p),
+                ("mask_ld", ctypes.c_int64), ("mask_kind", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("u", ctypes.c_void_p), ("ids", ctypes.c_void_p), ("status", ctypes.c_void_p)]
+
+
+def header_symbols(path: str = HEADER):
+    """Every function the C header declares (SSB_API ... name(...))."""
+    text = open(path).read()
+    return re.findall(r"SSB_API\s+[^;(]*?\b(ssb_\w+)\s*\(", text)
+
+
+_LIB = None
+
+
+def load_library(path: str = LIB_PATH):
+    """Loads the engine. Raises if it is not built — there is no fallback."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not os.path.exists(path):
+        raise FileNotFoundError(f"{path} is not built: run python speech.cpp_b200/speech_build.py")
+    lib = ctypes.CDLL(path)
+    vp, i32 = ctypes.c_void_p, ctypes.c_int32
+    lib.ssb_version.restype = ctypes.c_char_p
+    lib.ssb_last_error.restype = ctypes.c_char_p
+    lib.ssb_context_create.restype = ctypes.c_int
+    lib.ssb_context_create.argtypes = [i32, ctypes.POINTER(vp)]
+    lib.ssb_context_destroy.restype = ctypes.c_int
+    lib.ssb_context_destroy.argtypes = [vp]
+    lib.ssb_context_reserve.restype = ctypes.c_int
+    lib.ssb_context_reserve.argtypes = [vp, i32, i32]
+    lib.ssb_sample_rows.restype = ctypes.c_int
+    lib.ssb_sample_rows.argtypes = [vp, ctypes.POINTER(Rows), vp]
+    lib.ssb_candidates_rows.restype = ctypes.c_int
+    lib.ssb_candidates_rows.argtypes = [vp, ctypes.POINTER(Rows), i32, vp, vp, vp, vp, vp]
+    lib.ssb_sample_host.restype = ctypes.c_int
+    lib.ssb_sample_host.argtypes = [vp, ctypes.POINTER(Rows), vp]
+    _LIB = lib
+    return lib
+
+
+def _check(lib, status):
+    if status != OK:
+        raise SsbError(status, lib.ssb_last_error().decode())
+
+
+def _dptr(t):
+    """Device pointer of a torch tensor (or None)."""
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _hptr(a):
+    return None if a is None else ctypes.c_void_p(a.ctypes.data)
+
+
+class Sampler:
+    """One engine context on one CUDA device."""
+
+    def __init__(self, device: int = 0):
+        self.lib = load_library()
+        self.device = device
+        ctx = ctypes.c_void_p()
+        _check(self.lib, self.lib.ssb_context_create(device, ctypes.byref(ctx)))
+        self.ctx = ctx
+
+    def close(self):
+        if self.ctx:
+            self.lib.ssb_context_destroy(self.ctx)
+            self.ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def reserve(self, max_rows: int, max_vocab: int):
+        _check(self.lib, self.lib.ssb_context_reserve(self.ctx, max_rows, max_vocab))
+
+    @staticmethod
+    def _rows_struct(logits, p, history, history_len, mask, mask_kind, u, ids, status, row_params=None,
+                     max_top_k=0, host=False):
+        import torch  # noqa: F401  (only for dtype checks of device tensors)
+        r = Rows()
+        if host:
+            x = logits
+            r.dtype = BF16 if x.dtype == np.uint16 else F32
+            r.rows, r.vocab = x.shape
+            r.ld = x.strides[0] // x.itemsize
+            r.logits = x.ctypes.data
+            ptr = _hptr
+        else:
+            x = logits
+            r.dtype = BF16 if str(x.dtype) == "torch.bfloat16" else F32
+            if r.dtype == F32 and str(x.dtype) != "torch.float32":
+                raise TypeError("logits must be float32 or bfloat16")
+            r.rows, r.vocab = x.shape
+            r.ld = x.stride(0)
+            if x.stride(1) != 1:
+                raise ValueError("logits rows must be contiguous")
+            r.logits = x.data_ptr()
+            ptr = _dptr
+        r.max_top_k = max_top_k
+        r.params = p if p is not None else params()
+        r.row_params = ptr(row_params)
+        if history is not None:
+            r.history = ptr(history)
+            r.history_ld = history.shape[1]
+            r.history_len = ptr(history_len)
+        if mask is not None and mask_kind != MASK_NONE:
+            r.mask = ptr(mask)
+            r.mask_ld = 0 if mask.ndim == 1 else mask.shape[1]
+            r.mask_kind = mask_kind
+        r.u = ptr(u)
+        r.ids = ptr(ids)
+        r.status = ptr(status)
+        return r
+
+    def sample(self, logits, p: Params | None = None, history=None, history_len=None, mask=None,
+               mask_kind=MASK_NONE, u=None, row_params=None, max_top_k=0, ids=None, status=None, stream=None):
+        """Device tensors in, device tensors out (asynchronous on `stream`, a torch.cuda.Stream or None)."""
+        import torch
+        b = logits.shape[0]
+        if ids is None:
+            ids = torch.empty(b, dtype=torch.int32, device=logits.device)
+        if status is None:
+            status = torch.empty(b, dtype=torch.int32, device=logits.device)
+        r = self._rows_struct(logits, p, history, history_len, mask, mask_kind, u, ids, status, row_params, max_top_k)
+        s = None if stream is None else ctypes.c_void_p(stream.cuda_stream)
+        _check(self.lib, self.lib.ssb_sample_rows(self.ctx, ctypes.byref(r), s))
+        return ids, status
+
+    def candidates(self, logits, p: Params | None = None, history=None, history_len=None, mask=None,
+                   mask_kind=MASK_NONE, u=None, row_params=None, max_top_k=0, cap=64, processed=True, stream=None):
+        """The parity export: ids, status, tokens [B,cap], weights [B,cap], count [B], processed [B,V]."""
+        import torch
+        b, v = logits.shape
+        dev = logits.device
+        ids = torch.empty(b, dtype=torch.int32, device=dev)
+        status = torch.empty(b, dtype=torch.int32, device=dev)
+        tokens = torch.full((b, max(cap, 1)), -1, dtype=torch.int32, device=dev)
+        weights = torch.zeros((b, max(cap, 1)), dtype=torch.float64, device=dev)
+        count = torch.zeros(b, dtype=torch.int32, device=dev)
+        proc = torch.empty((b, v), dtype=torch.float32, device=dev) if processed else None
+        r = self._rows_struct(logits, p, history, history_len, mask, mask_kind, u, ids, status, row_params, max_top_k)
+        s = None if stream is None else ctypes.c_void_p(stream.cuda_stream)
+        _check(self.lib, self.lib.ssb_candidates_rows(self.ctx, ctypes.byref(r), cap, _dptr(tokens), _dptr(weights),
+                                                     _dptr(count), _dptr(proc), s))
+        return ids, status, tokens, weights, count, proc
+
+    def sample_host(self, logits, p: Params | None = None, history=None, history_len=None, mask=None,
+                    mask_kind=MASK_NONE, u=None, row_params=None, max_top_k=0, ids=None, status=None, stream=None):
+        """Host (numpy) buffers in and out; copies happen inside the call, which waits for the result."""
+        b = logits.shape[0]
+        ids = np.empty(b, np.int32) if ids is None else ids
+        status = np.empty(b, np.int32) if status is None else status
+        r = self._rows_struct(logits, p, history, history_len, mask, mask_kind, u, ids, status, row_params,
+                              max_top_k, host=True)
+        s = None if stream is None else ctypes.c_void_p(stream.cuda_stream)
+        _check(self.lib, self.lib.ssb_sample_host(self.ctx, ctypes.byref(r), s))
+        return ids, status
