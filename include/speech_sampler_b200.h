@@ -49,6 +49,8 @@ typedef enum ssb_status {
  *   NO_FINITE_LOGIT      -> std::runtime_error("no token has a finite logit to pick from")  sampler.cpp:49
  *   NON_FINITE_INPUT     -> Error(Device, ...)  a NaN among the restricted logits (haru/sampler.cpp:21-23)
  *   INVALID_ROW          -> a row whose own parameters exceed the launch's bounds (ssb_rows.max_top_k)
+ *   DEVICE_TIMEOUT       -> Error(Device, ...): the row's logits did not arrive in shared memory within
+ *                           the kernel's bounded wait (a device fault; never expected)
  */
 typedef enum ssb_row_status {
     SSB_ROW_OK = 0,
@@ -56,7 +58,8 @@ typedef enum ssb_row_status {
     SSB_ROW_TEMPERATURE_OVERFLOW = 2,
     SSB_ROW_NO_FINITE_LOGIT = 3,
     SSB_ROW_NON_FINITE_INPUT = 4,
-    SSB_ROW_INVALID_ROW = 5
+    SSB_ROW_INVALID_ROW = 5,
+    SSB_ROW_DEVICE_TIMEOUT = 6
 } ssb_row_status;
 
 typedef enum ssb_dtype { SSB_F32 = 0, SSB_BF16 = 1 } ssb_dtype;

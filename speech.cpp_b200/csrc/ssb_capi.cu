@@ -174,18 +174,18 @@ ssb_status run(ssb_context * ctx, const ssb_rows * r, const Debug * dbg, cudaStr
     const int mode = plan.mode;
     const int es = bf16 ? 2 : 4;
     const bool vec = (reinterpret_cast<uintptr_t>(r->logits) % 16 == 0) && ((r->ld * es) % 16 == 0);
-    const int g = vec ? 16 / es : 1;
     const int kb = std::max(1, plan.k_bound);
     a.k_bound = kb;
     ssb::StreamArgs sa{};
     sa.r = a;
-    sa.hist_slots = r->history ? ssb::next_pow2((int) std::max<int64_t>(2, r->history_ld)) : 0;
-    sa.cap = mode == 1 ? (int) div_up(ssb::kStreamThreads * g + kb + std::max(1024, kb), 32) * 32 : 0;
+    sa.hist_slots = r->history ? ssb::next_pow2((int) std::max<int64_t>(4, 2 * r->history_ld)) : 0;  // hash, load <= 1/2
+    sa.cap = mode == 1 ? (int) div_up(kb + std::max(1024, kb), 32) * 32 : 0;
     sa.sel_slots = mode == 1 ? ssb::next_pow2(std::max(kb, 2)) : 0;
     int & occ = ctx->occupancy[mode][bf16][vec];
     if (occ == 0) {
         const int full_chunk = (int) div_up(r->vocab, 32) * 32;
-        occ = ssb::stream_blocks_per_sm(mode, bf16, vec, ssb::stream_smem_bytes(mode, full_chunk, sa.hist_slots, sa.cap, sa.sel_slots));
+        occ = ssb::stream_blocks_per_sm(mode, bf16, vec,
+                                        ssb::stream_smem_bytes(mode, vec, full_chunk, sa.hist_slots, sa.cap, sa.sel_slots));
         if (occ <= 0) return fail(SSB_DEVICE, "the streaming kernel does not fit on this device");
     }
     const int slots = std::min(ctx->max_slots, ctx->sm_count * occ);

@@ -222,10 +222,12 @@ struct SelectState {
 };
 
 // Selects the `k` largest composites among n produced by key_of(i) (i in [0, n)), 1 <= k <= n.
-// Afterwards an element is selected iff (key >> st.shift) >= (st.prefix >> st.shift): digits of 8
-// bits from the top, stopping as soon as the bucket holding the k-th is taken whole. Block-wide.
+// Afterwards an element is selected iff (key >> st.shift) >= (st.prefix >> st.shift), equivalently
+// key >= st.prefix (its bits below st.shift are zero): digits of 8 bits from the top, stopping as soon
+// as the bucket holding the k-th is taken whole, or after `max_rounds` digits — then the selection
+// holds at least k elements (the k best and the rest of their bucket). Block-wide.
 template <typename KeyOf>
-__device__ inline void radix_select(int n, int k, KeyOf key_of, SelectState & st) {
+__device__ inline void radix_select(int n, int k, KeyOf key_of, SelectState & st, int max_rounds = 8) {
     if (threadIdx.x == 0) {
         st.prefix = 0;
         st.shift = 64;
@@ -284,7 +286,7 @@ __device__ inline void radix_select(int n, int k, KeyOf key_of, SelectState & st
                 st.prefix = prefix | ((uint64_t) digit << shift);
                 st.remaining = rem - (int) above;
                 st.shift = shift;
-                st.done = (c[j] == (uint32_t) (rem - (int) above)) || shift == 0;
+                st.done = (c[j] == (uint32_t) (rem - (int) above)) || shift <= 64 - 8 * max_rounds;
             }
         }
         __syncthreads();
@@ -295,6 +297,35 @@ __device__ inline void radix_select(int n, int k, KeyOf key_of, SelectState & st
 
 __device__ __forceinline__ bool selected(uint64_t c, const SelectState & st) {
     return st.shift >= 64 ? true : (c >> st.shift) >= (st.prefix >> st.shift);
+}
+
+// Descending bitonic sort of the 32*R u64 held by one warp, element r*32 + lane in x[r]. Warp-wide,
+// registers and shuffles only.
+template <int R>
+__device__ __forceinline__ void warp_sort_desc(uint64_t (&x)[R]) {
+    const int lane = lane_id();
+#pragma unroll
+    for (int size = 2; size <= 32 * R; size <<= 1) {
+#pragma unroll
+        for (int j = size >> 1; j > 0; j >>= 1) {
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const int i = r * 32 + lane;
+                const bool desc = (i & size) == 0;
+                if (j >= 32) {
+                    const int rp = r ^ (j >> 5);
+                    if (rp > r) {
+                        const uint64_t a = x[r], b = x[rp];
+                        if ((a < b) == desc) x[r] = b, x[rp] = a;
+                    }
+                } else {
+                    const uint64_t o = shfl_xor(x[r], j);
+                    const bool keep_max = ((lane & j) == 0) == desc;
+                    x[r] = keep_max ? (x[r] > o ? x[r] : o) : (x[r] < o ? x[r] : o);
+                }
+            }
+        }
+    }
 }
 
 // Descending bitonic sort of n (a power of two) u64 in shared memory. Block-wide.

@@ -44,8 +44,8 @@ struct StreamArgs {
     RowsArgs r;
     int splits;
     int chunk;       // columns per split, a multiple of 32
-    int cap;         // candidate buffer entries per CTA (top-k mode)
-    int hist_slots;  // shared slots for in-range history ids (power of two >= history_ld)
+    int cap;         // candidate buffer entries per CTA (top-k mode): k_bound + slack
+    int hist_slots;  // shared hash-table slots for in-range history ids (power of two >= 2 history_ld)
     int sel_slots;   // shared slots for the selected candidates (>= k_bound)
     uint64_t * part_cand;  // [rows * splits * k_bound] composites
     int32_t * part_n;      // [rows * splits]
@@ -61,7 +61,7 @@ size_t small_smem_bytes(int vocab, int k_bound);
 cudaError_t launch_small(const SmallArgs & a, bool bf16, bool debug, cudaStream_t stream);
 
 // mode 0: every row greedy (argmax); mode 1: top-k draw (greedy rows as top-1 of unscaled logits)
-size_t stream_smem_bytes(int mode, int chunk, int hist_slots, int cap, int sel_slots);
+size_t stream_smem_bytes(int mode, bool vec, int chunk, int hist_slots, int cap, int sel_slots);
 cudaError_t launch_stream(const StreamArgs & a, int mode, bool bf16, bool vec, bool debug, cudaStream_t stream);
 int stream_blocks_per_sm(int mode, bool bf16, bool vec, size_t smem);
 

@@ -24,7 +24,8 @@ LIB_PATH = os.path.join(PKG, "libspeech_sampler_b200.so")
 HEADER = os.path.join(ROOT, "include", "speech_sampler_b200.h")
 
 OK, INVALID_ARGUMENT, OUT_OF_RANGE, DEVICE, OUT_OF_MEMORY = range(5)
-ROW_OK, ROW_PENALTY_OVERFLOW, ROW_TEMPERATURE_OVERFLOW, ROW_NO_FINITE_LOGIT, ROW_NON_FINITE_INPUT, ROW_INVALID_ROW = range(6)
+(ROW_OK, ROW_PENALTY_OVERFLOW, ROW_TEMPERATURE_OVERFLOW, ROW_NO_FINITE_LOGIT, ROW_NON_FINITE_INPUT, ROW_INVALID_ROW,
+ ROW_DEVICE_TIMEOUT) = range(7)
 F32, BF16 = 0, 1
 MASK_NONE, MASK_BAN, MASK_ALLOW = 0, 1, 2
 SMALL_VOCAB = 8192
