@@ -30,6 +30,8 @@ struct ssb_context {
     cudaEvent_t done = nullptr;
     // occupancy of the streaming kernel per (mode, bf16, vec), measured at the row's full width
     int occupancy[2][2][2] = {};
+    // occupancy of the selection kernel per (warp-queue width class, bf16)
+    int occ_select[4][2] = {};
 };
 
 namespace {
@@ -181,11 +183,15 @@ ssb_status run(ssb_context * ctx, const ssb_rows * r, const Debug * dbg, cudaStr
     sa.hist_slots = r->history ? ssb::next_pow2((int) std::max<int64_t>(4, 2 * r->history_ld)) : 0;  // hash, load <= 1/2
     sa.cap = mode == 1 ? (int) div_up(kb + std::max(1024, kb), 32) * 32 : 0;
     sa.sel_slots = mode == 1 ? ssb::next_pow2(std::max(kb, 2)) : 0;
-    int & occ = ctx->occupancy[mode][bf16][vec];
+    // aligned rows with a small top-k (or all greedy) take the warp-specialized selection kernel
+    const bool use_select = vec && (mode == 0 || kb <= ssb::kSelectMaxK);
+    const int kw = use_select ? ssb::select_kw(kb, mode == 0) : -1;
+    int & occ = use_select ? ctx->occ_select[kw == 0 ? 0 : (kw == 1 ? 1 : (kw == 2 ? 2 : 3))][bf16] : ctx->occupancy[mode][bf16][vec];
     if (occ == 0) {
         const int full_chunk = (int) div_up(r->vocab, 32) * 32;
-        occ = ssb::stream_blocks_per_sm(mode, bf16, vec,
-                                        ssb::stream_smem_bytes(mode, vec, full_chunk, sa.hist_slots, sa.cap, sa.sel_slots));
+        occ = use_select ? ssb::select_blocks_per_sm(kw, bf16, ssb::select_smem_bytes(kw, full_chunk, sa.hist_slots, sa.sel_slots))
+                         : ssb::stream_blocks_per_sm(mode, bf16, vec,
+                                                     ssb::stream_smem_bytes(mode, vec, full_chunk, sa.hist_slots, sa.cap, sa.sel_slots));
         if (occ <= 0) return fail(SSB_DEVICE, "the streaming kernel does not fit on this device");
     }
     const int slots = std::min(ctx->max_slots, ctx->sm_count * occ);
@@ -204,7 +210,7 @@ ssb_status run(ssb_context * ctx, const ssb_rows * r, const Debug * dbg, cudaStr
         sa.counters = ctx->counters;
     }
     if ((int64_t) r->rows * splits > INT32_MAX) return fail(SSB_OUT_OF_RANGE, "too many rows for one launch");
-    e = ssb::launch_stream(sa, mode, bf16, vec, debug, stream);
+    e = use_select ? ssb::launch_select(sa, kw, bf16, debug, stream) : ssb::launch_stream(sa, mode, bf16, vec, debug, stream);
     if (e != cudaSuccess) return cuda_fail(e, "streaming kernel launch");
     return ok();
 }

@@ -65,4 +65,12 @@ size_t stream_smem_bytes(int mode, bool vec, int chunk, int hist_slots, int cap,
 cudaError_t launch_stream(const StreamArgs & a, int mode, bool bf16, bool vec, bool debug, cudaStream_t stream);
 int stream_blocks_per_sm(int mode, bool bf16, bool vec, size_t smem);
 
+// Warp-specialized selection kernel (ssb_select.cu) for 16-byte-aligned rows: kw = 0 for all-greedy
+// batches, else the warp-queue width (1, 2 or 4 registers: top-k up to 32, 64, 128).
+constexpr int kSelectMaxK = 128;
+int select_kw(int k_bound, bool all_greedy);
+size_t select_smem_bytes(int kw, int chunk, int hist_slots, int sel_slots);
+int select_blocks_per_sm(int kw, bool bf16, size_t smem);
+cudaError_t launch_select(const StreamArgs & a, int kw, bool bf16, bool debug, cudaStream_t stream);
+
 }  // namespace ssb
