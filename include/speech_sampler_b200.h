@@ -166,6 +166,18 @@ SSB_API ssb_status ssb_candidates_rows(ssb_context *ctx, const ssb_rows *rows, i
  */
 SSB_API ssb_status ssb_sample_host(ssb_context *ctx, const ssb_rows *rows, void *stream);
 
+/*
+ * ssb_sample_rows without a context and without any device allocation, for callers that cannot call
+ * cudaMalloc (a runtime that owns all device memory through its own pool, or a process that must not
+ * grow its footprint or synchronize the device on its decode path). No counterpart in the reference.
+ * Pointers in `rows` are device pointers, as for ssb_sample_rows. The split-row scratch is a fixed
+ * array of about 2.03 MiB inside the library, held by every GPU that loads it; the first call on each
+ * device looks up its address (make it before any stream capture). Takes rows of more than
+ * SSB_SMALL_VOCAB tokens, 16-byte aligned, with a top-k of at most 128 or greedy; anything else is
+ * SSB_OUT_OF_RANGE. Calls share the array: calls that overlap on the GPU race and must not be made.
+ */
+SSB_API ssb_status ssb_sample_rows_noalloc(const ssb_rows *rows, void *stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

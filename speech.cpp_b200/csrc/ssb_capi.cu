@@ -234,6 +234,11 @@ ssb_status wait_stream(ssb_context * ctx, cudaStream_t stream, double timeout_s)
 
 }  // namespace
 
+namespace ssb {
+// Lets other entry points of the library report through ssb_last_error().
+void set_last_error(const std::string & message) { g_error = message; }
+}  // namespace ssb
+
 extern "C" {
 
 const char * ssb_version(void) { return "0.1.0"; }
