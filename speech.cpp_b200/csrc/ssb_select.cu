@@ -37,12 +37,13 @@ namespace ssb {
 namespace {
 
 constexpr int kStageBytes = 16384;
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;  // + the producer warp
 constexpr int kGroupsPerThread = kStageBytes / 16 / kConsumers;
 constexpr int kWarpBuf = 128;              // candidate buffer entries per consumer warp
+constexpr int kDefer = 64;                 // deferred flagged groups per consumer warp
 constexpr uint32_t kWaitLimit = 1u << 22;  // bounded mbarrier polls
 constexpr uint32_t kLockLimit = 1u << 22;  // bounded lock attempts
 
@@ -159,19 +160,19 @@ struct Shared {
 
 // Sorts a warp's candidate buffer and merges its best into the CTA queue `gq` under the lock; raises
 // the threshold to the queue's k-th entry. Warp-wide; not inlined, so one copy of the networks exists.
-template <int QN>
+template <int QN, int R>
 __device__ __noinline__ void publish(const uint64_t * wbuf, int wn, uint64_t * gq, int k, Shared * sh) {
     const int lane = lane_id();
-    uint64_t x[kWarpBuf / 32];
+    uint64_t x[R];
 #pragma unroll
-    for (int r = 0; r < kWarpBuf / 32; r++) {
+    for (int r = 0; r < R; r++) {
         const int i = r * 32 + lane;
         x[r] = i < wn ? wbuf[i] : 0ull;
     }
-    warp_sort_desc<kWarpBuf / 32>(x);
+    warp_sort_desc<R>(x);
     uint64_t t[QN];
 #pragma unroll
-    for (int r = 0; r < QN; r++) t[r] = x[r];
+    for (int r = 0; r < QN; r++) t[r] = r < R ? x[r < R ? r : 0] : 0ull;
     int got = 0;
     if (lane == 0) {
         for (uint32_t n = 0; n < kLockLimit; n++) {
@@ -291,6 +292,8 @@ __global__ void __launch_bounds__(kThreads, 2) select_rows_kernel(const StreamAr
     uint64_t * s_wbuf = reinterpret_cast<uint64_t *>(s_hval + sa.hist_slots);  // [kConsumerWarps][kWarpBuf]
     uint64_t * s_queue = s_wbuf + kConsumerWarps * kWarpBuf;                    // [32*QN]
     uint64_t * s_sel = s_queue + 32 * QN;                                      // [max(sel_slots, 32*QN)]
+    uint4 * s_draw = reinterpret_cast<uint4 *>(s_sel + (sa.sel_slots > 32 * QN ? sa.sel_slots : 32 * QN));  // [8][kDefer]
+    int * s_dcol = reinterpret_cast<int *>(s_draw + kConsumerWarps * kDefer);                               // [8][kDefer]
 
     const TIn * src = reinterpret_cast<const TIn *>(a.logits) + (int64_t) row * a.ld;
     const char * gsrc = reinterpret_cast<const char *>(src + c0);
@@ -397,18 +400,22 @@ __global__ void __launch_bounds__(kThreads, 2) select_rows_kernel(const StreamAr
             }
         }
     };
-    // appends each lane's candidate `cv` (where `has`) to the warp buffer; publishes when it could overflow
+    // merges the warp's buffered candidates into the CTA queue (sorting only as many as it holds)
+    auto flush = [&]() {
+        __syncwarp();
+        if (wn <= 32) publish<QN, 1>(wbuf, wn, s_queue, k, &sh);
+        else if (wn <= 64) publish<QN, 2>(wbuf, wn, s_queue, k, &sh);
+        else publish<QN, 4>(wbuf, wn, s_queue, k, &sh);
+        wn = 0;
+        refresh();
+    };
+    // appends each lane's candidate `cv` (where `has`) to the warp buffer; flushes when it could overflow
     auto append = [&](bool has, uint64_t cv) {
         const unsigned m = __ballot_sync(0xffffffffu, has);
         if (!m) return;
         if (has) wbuf[wn + __popc(m & ((1u << lane) - 1u))] = cv;
         wn += __popc(m);
-        if (wn > kWarpBuf - 32) {
-            __syncwarp();
-            publish<QN>(wbuf, wn, s_queue, k, &sh);
-            wn = 0;
-            refresh();
-        }
+        if (wn > kWarpBuf - 32) flush();
     };
     // top-k: the per-element test of a candidate (restricted value v at column col), warp-uniform
     auto element = [&](bool valid, float v, int col) {
@@ -422,6 +429,36 @@ __global__ void __launch_bounds__(kThreads, 2) select_rows_kernel(const StreamAr
         }
         append(has, cv);
     };
+    // one flagged group per lane (has): widen, restrict, fold into the statistics, test its elements
+    auto process_item = [&](bool has, const uint4 & raw, int col0) {
+        float v[G];
+        uint32_t sb = 0;
+        if (has) {
+            Elem<TIn>::unpack(raw, v);
+            sb = special ? special_bits<G>(c, col0) : 0u;
+        } else {
+#pragma unroll
+            for (int e = 0; e < G; e++) v[e] = -kInf;
+        }
+        uint64_t lbest = 0;
+#pragma unroll
+        for (int e = 0; e < G; e++) {
+            if (has) {
+                v[e] = restrict1(c, v[e], col0 + e, sb, e);
+                acc = max_nan(acc, v[e]);
+                if (kDebug && c.processed) c.processed[col0 + e] = v[e];
+            }
+            if (KW == 0) {
+                if (has && v[e] == v[e] && v[e] >= thr) {
+                    const uint64_t cv = composite(v[e], (uint32_t) (col0 + e));
+                    lbest = cv > lbest ? cv : lbest;
+                }
+            } else {
+                element(has, v[e], col0 + e);
+            }
+        }
+        return lbest;
+    };
     // greedy: folds each lane's best composite of an item into the CTA's best, once per warp
     auto greedy_fold = [&](uint64_t lbest) {
         const uint64_t m = warp_max_u64(lbest);
@@ -432,6 +469,23 @@ __global__ void __launch_bounds__(kThreads, 2) select_rows_kernel(const StreamAr
             thr = b > thr ? b : thr;
         }
     };
+
+    // the deferred flagged groups of this warp, 32 per pass; then the candidates reach the CTA queue
+    int dn = 0;  // warp-uniform count of deferred groups
+    auto process_deferred = [&]() {
+        __syncwarp();
+        for (int base = 0; base < dn; base += 32) {  // warp-uniform
+            const int item = base + lane;
+            const bool has = item < dn;
+            const uint4 raw = has ? s_draw[warp * kDefer + item] : make_uint4(0, 0, 0, 0);
+            const int col0 = has ? s_dcol[warp * kDefer + item] : c0;
+            process_item(has, raw, col0);
+        }
+        dn = 0;
+        if (wn >= 32) flush();
+        __syncwarp();
+    };
+    auto consumer_sync = [&]() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory"); };
 
     if (producer) {
         if (lane == 0) {
@@ -492,76 +546,85 @@ __global__ void __launch_bounds__(kThreads, 2) select_rows_kernel(const StreamAr
                     }
                 }
             }
-            // the first stage seeds the threshold with the k-th largest group maximum of the warp
-            if (KW > 0 && st == 0 && c.fast && k <= 32 * kGroupsPerThread) {
+            // top-k: the first stage seeds the CTA's threshold with the k-th largest of its group maxima
+            // (k elements are at least that large; a positive temperature keeps the logits' order)
+            if (KW > 0 && st == 0 && c.fast) {
                 uint64_t seeds[kGroupsPerThread];
 #pragma unroll
                 for (int j = 0; j < kGroupsPerThread; j++)
                     seeds[j] = (uint64_t) order_key(gmax[j] == gmax[j] ? gmax[j] : -kInf) << 32;
                 warp_sort_desc<kGroupsPerThread>(seeds);
-                const float s0raw = composite_value(warp_get<kGroupsPerThread>(seeds, k - 1));
-                if (s0raw > -kInf) {
-                    const float s0 = c.scale ? __fdiv_rn(s0raw, c.tscale) : s0raw;
-                    const uint64_t t0 = (uint64_t) order_key(s0) << 32;
-                    if (lane == 0) atomicMax(reinterpret_cast<unsigned long long *>(&sh.theta), (unsigned long long) t0);
-                    if (t0 > theta) theta = t0, thr = raw_bound(s0, c.tscale, c.fast);
-                    flagged = 0;
 #pragma unroll
-                    for (int j = 0; j < kGroupsPerThread; j++) {
-                        const int g = j * kConsumers + tid;
-                        if (g < sgroups)
-                            flagged |= (uint32_t) (kDebug || gmax[j] >= thr || gmax[j] != gmax[j] ||
-                                                   (special && special_bits<G>(c, sbase + g * G) != 0))
-                                       << j;
+                for (int r = 0; r < QN; r++) s_wbuf[warp * kWarpBuf + r * 32 + lane] = seeds[r];
+                consumer_sync();
+                if (warp == 0) {
+                    uint64_t q[QN];
+#pragma unroll
+                    for (int r = 0; r < QN; r++) q[r] = s_wbuf[r * 32 + lane];
+                    for (int w = 1; w < kConsumerWarps; w++) {
+                        uint64_t t[QN];
+#pragma unroll
+                        for (int r = 0; r < QN; r++) t[r] = s_wbuf[w * kWarpBuf + r * 32 + lane];
+                        warp_merge_sorted<QN>(q, t);
+                    }
+                    const float s0raw = composite_value(warp_get<QN>(q, k - 1));
+                    if (lane == 0 && s0raw > -kInf) {
+                        const float s0 = c.scale ? __fdiv_rn(s0raw, c.tscale) : s0raw;
+                        atomicMax(reinterpret_cast<unsigned long long *>(&sh.theta), (unsigned long long) order_key(s0) << 32);
                     }
                 }
+                consumer_sync();
+                refresh();
+                flagged = 0;
+#pragma unroll
+                for (int j = 0; j < kGroupsPerThread; j++) {
+                    const int g = j * kConsumers + tid;
+                    if (g < sgroups)
+                        flagged |= (uint32_t) (kDebug || gmax[j] >= thr || gmax[j] != gmax[j] ||
+                                               (special && special_bits<G>(c, sbase + g * G) != 0))
+                                   << j;
+                }
             }
-            // slow path: the warp's flagged groups as a work list, one group per lane
+            // the warp's flagged groups
             unsigned bl[kGroupsPerThread];
             int total = 0;
 #pragma unroll
             for (int j = 0; j < kGroupsPerThread; j++) bl[j] = __ballot_sync(0xffffffffu, (flagged >> j) & 1u), total += __popc(bl[j]);
-            for (int base = 0; base < total; base += 32) {  // warp-uniform
-                const int item = base + lane;
-                const bool has = item < total;
-                int jj = 0, r = item;
-                const int n0 = __popc(bl[0]), n1 = __popc(bl[1]), n2 = __popc(bl[2]);
-                if (r >= n0) { r -= n0; jj = 1; if (r >= n1) { r -= n1; jj = 2; if (r >= n2) { r -= n2; jj = 3; } } }
-                const unsigned bj = jj == 0 ? bl[0] : (jj == 1 ? bl[1] : (jj == 2 ? bl[2] : bl[3]));
-                const int srcl = has ? (int) __fns(bj, 0, r + 1) : 0;
-                const int g = jj * kConsumers + warp * 32 + srcl;
-                const int col0 = sbase + g * G;
-                float v[G];
-                uint32_t sb = 0;
-                if (has) {
-                    Elem<TIn>::unpack(stage[g], v);
-                    sb = special ? special_bits<G>(c, col0) : 0u;
-                } else {
+            if (KW > 0 && total > 0 && dn + total > kDefer) process_deferred();
+            if (KW > 0 && total > 0 && total <= kDefer) {
+                // top-k: defer them (raw bytes and column) and take them 32 at a time
+                int off = 0;
 #pragma unroll
-                    for (int e = 0; e < G; e++) v[e] = -kInf;
-                }
-                uint64_t lbest = 0;
-#pragma unroll
-                for (int e = 0; e < G; e++) {
-                    if (has) {
-                        v[e] = restrict1(c, v[e], col0 + e, sb, e);
-                        acc = max_nan(acc, v[e]);
-                        if (kDebug && c.processed) c.processed[col0 + e] = v[e];
+                for (int j = 0; j < kGroupsPerThread; j++) {
+                    if ((flagged >> j) & 1u) {
+                        const int pos = dn + off + __popc(bl[j] & ((1u << lane) - 1u));
+                        const int g = j * kConsumers + tid;
+                        s_draw[warp * kDefer + pos] = stage[g];
+                        s_dcol[warp * kDefer + pos] = sbase + g * G;
                     }
-                    if (KW == 0) {
-                        if (has && v[e] == v[e] && v[e] >= thr) {
-                            const uint64_t cv = composite(v[e], (uint32_t) (col0 + e));
-                            lbest = cv > lbest ? cv : lbest;
-                        }
-                    } else {
-                        element(has, v[e], col0 + e);
-                    }
+                    off += __popc(bl[j]);
                 }
-                if (KW == 0) greedy_fold(lbest);
+                dn += total;
+                if (dn >= 32) process_deferred();
+            } else {
+                // greedy, or a flood larger than the deferred list: the groups straight from the stage
+                for (int base = 0; base < total; base += 32) {  // warp-uniform
+                    const int item = base + lane;
+                    const bool has = item < total;
+                    int jj = 0, r = item;
+                    const int n0 = __popc(bl[0]), n1 = __popc(bl[1]), n2 = __popc(bl[2]);
+                    if (r >= n0) { r -= n0; jj = 1; if (r >= n1) { r -= n1; jj = 2; if (r >= n2) { r -= n2; jj = 3; } } }
+                    const unsigned bj = jj == 0 ? bl[0] : (jj == 1 ? bl[1] : (jj == 2 ? bl[2] : bl[3]));
+                    const int srcl = has ? (int) __fns(bj, 0, r + 1) : 0;
+                    const int g = jj * kConsumers + warp * 32 + srcl;
+                    const uint64_t lbest = process_item(has, has ? stage[g] : make_uint4(0, 0, 0, 0), sbase + g * G);
+                    if (KW == 0) greedy_fold(lbest);
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_empty[slot]);
         }
+        if (KW > 0 && dn > 0) process_deferred();
         // columns past the last whole 16-byte group: one per lane
         for (int base = c0 + nvec * G; base < c1; base += kConsumers) {  // warp-uniform trip count
             const int col = base + tid;
@@ -577,7 +640,7 @@ __global__ void __launch_bounds__(kThreads, 2) select_rows_kernel(const StreamAr
             if (KW == 0) greedy_fold(ok && v == v && v >= thr ? composite(v, (uint32_t) col) : 0ull);
             else element(ok, v, col);
         }
-        if (KW > 0 && wn > 0) publish<QN>(wbuf, wn, s_queue, k, &sh);
+        if (KW > 0 && wn > 0) flush();
         if (KW == 0 && lane == 0)
             atomicMax(reinterpret_cast<unsigned long long *>(&sh.best), (unsigned long long) theta);
     }
@@ -737,7 +800,7 @@ size_t select_smem_bytes(int kw, int chunk, int hist_slots, int sel_slots) {
     const int qn = kw > 0 ? kw : 1;
     return (size_t) kStages * kStageBytes + hwords * 4 + (size_t) hist_slots * 8 +
            (size_t) kConsumerWarps * kWarpBuf * 8 + (size_t) 32 * qn * 8 +
-           (size_t) (sel_slots > 32 * qn ? sel_slots : 32 * qn) * 8;
+           (size_t) (sel_slots > 32 * qn ? sel_slots : 32 * qn) * 8 + (size_t) kConsumerWarps * kDefer * (16 + 4);
 }
 
 int select_blocks_per_sm(int kw, bool bf16, size_t smem) {
