@@ -189,7 +189,7 @@ ssb_status run(ssb_context * ctx, const ssb_rows * r, const Debug * dbg, cudaStr
     int & occ = use_select ? ctx->occ_select[kw == 0 ? 0 : (kw == 1 ? 1 : (kw == 2 ? 2 : 3))][bf16] : ctx->occupancy[mode][bf16][vec];
     if (occ == 0) {
         const int full_chunk = (int) div_up(r->vocab, 32) * 32;
-        occ = use_select ? ssb::select_blocks_per_sm(kw, bf16, ssb::select_smem_bytes(kw, full_chunk, sa.hist_slots, sa.sel_slots))
+        occ = use_select ? ssb::select_blocks_per_sm(kw, bf16, ssb::select_smem_bytes(kw, bf16, full_chunk, sa.hist_slots, sa.sel_slots))
                          : ssb::stream_blocks_per_sm(mode, bf16, vec,
                                                      ssb::stream_smem_bytes(mode, vec, full_chunk, sa.hist_slots, sa.cap, sa.sel_slots));
         if (occ <= 0) return fail(SSB_DEVICE, "the streaming kernel does not fit on this device");

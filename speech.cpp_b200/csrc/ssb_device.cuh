@@ -377,6 +377,41 @@ struct RowOut {
     int cap;
 };
 
+// Sum of w[0 .. n) added in index order (the reference's sequential accumulation); the loads of each
+// block of 8 are issued before its additions.
+__device__ __forceinline__ double ordered_sum(const double * w, int n) {
+    double s = 0.0;
+    int i = 0;
+    for (; i + 8 <= n; i += 8) {
+        double v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = w[i + j];
+#pragma unroll
+        for (int j = 0; j < 8; j++) s = __dadd_rn(s, v[j]);
+    }
+    for (; i < n; i++) s = __dadd_rn(s, w[i]);
+    return s;
+}
+
+// Index of the first i < n at which the running sum of w[0 .. i] (in index order) passes the limit
+// (`strict`: > limit, else >= limit); n when it never does.
+__device__ __forceinline__ int first_crossing(const double * w, int n, double limit, bool strict) {
+    double s = 0.0;
+    for (int i = 0; i < n; i += 8) {
+        double v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = i + j < n ? w[i + j] : 0.0;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            if (i + j < n) {
+                s = __dadd_rn(s, v[j]);
+                if (strict ? s > limit : s >= limit) return i + j;
+            }
+        }
+    }
+    return n;
+}
+
 // The reference's softmax, top-p and pick over the k candidates sorted by composite (descending):
 // weights exp((double)s - max) summed in order (qwen3-tts/sampler.cpp:85-87), normalized, cut at the
 // first cumulative share >= top_p (:88-99), then pick() (sampling.cpp:9-19): each a sequence of
@@ -394,51 +429,44 @@ __device__ inline void finalize_draw(const uint64_t * sorted, int k, const RowPa
         }
         return;
     }
+    __shared__ double s_sum;
+    __shared__ int s_keep;
+    // softmax (qwen3-tts/sampler.cpp:80-87): exp of the shifted logits in parallel, their sum in order
     for (int i = threadIdx.x; i < k; i += blockDim.x) w[i] = exp((double) composite_value(sorted[i]) - (double) max_logit);
     __syncthreads();
-    __shared__ double s_sum;
-    if (threadIdx.x == 0) {
-        double sum = 0;
-        for (int i = 0; i < k; i++) sum = __dadd_rn(sum, w[i]);
-        s_sum = sum;
-    }
+    if (threadIdx.x == 0) s_sum = ordered_sum(w, k);
     __syncthreads();
     const double sum = s_sum;
     for (int i = threadIdx.x; i < k; i += blockDim.x) w[i] = __ddiv_rn(w[i], sum);
     __syncthreads();
+    // top-p cut (:88-99): keep through the first cumulative share >= top_p; then pick()'s total
     if (threadIdx.x == 0) {
         int keep = k;
         if (p.top_p < 1.0f) {
-            double cumulative = 0;
-            keep = 0;
-            while (keep < k) {
-                cumulative = __dadd_rn(cumulative, w[keep++]);
-                if (cumulative >= (double) p.top_p) break;
-            }
+            const int at = first_crossing(w, k, (double) p.top_p, false);
+            keep = at < k ? at + 1 : k;
         }
-        double s2 = 0;
-        for (int i = 0; i < keep; i++) s2 = __dadd_rn(s2, w[i]);
-        int chosen = keep - 1;
-        double cumulative = 0;
-        for (int i = 0; i < keep - 1; i++) {
-            cumulative = __dadd_rn(cumulative, __ddiv_rn(w[i], s2));
-            if (cumulative > u) {
-                chosen = i;
-                break;
-            }
-        }
-        *out.id = (int32_t) composite_index(sorted[chosen]);
-        *out.status = SSB_ROW_OK;
-        if (out.count) *out.count = keep;
-        s_sum = (double) keep;  // hand the kept count to the other threads
+        s_keep = keep;
+        s_sum = ordered_sum(w, keep);
     }
+    __syncthreads();
+    const int keep = s_keep;
+    const double s2 = s_sum;
     if (out.tokens) {
-        __syncthreads();
-        const int keep = (int) s_sum;
         for (int i = threadIdx.x; i < keep && i < out.cap; i += blockDim.x) {
             out.tokens[i] = (int32_t) composite_index(sorted[i]);
             out.weights[i] = w[i];
         }
+        __syncthreads();
+    }
+    // pick() (sampling.cpp:9-19): the renormalized shares in parallel, the first cumulative > u in order
+    for (int i = threadIdx.x; i < keep - 1; i += blockDim.x) w[i] = __ddiv_rn(w[i], s2);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int chosen = first_crossing(w, keep - 1, u, true);  // keep - 1 (the last) when none passes
+        *out.id = (int32_t) composite_index(sorted[chosen]);
+        *out.status = SSB_ROW_OK;
+        if (out.count) *out.count = keep;
     }
 }
 

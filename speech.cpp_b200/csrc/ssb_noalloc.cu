@@ -162,7 +162,7 @@ extern "C" ssb_status ssb_sample_rows_noalloc(const ssb_rows * r, void * stream_
     sa.hist_slots = r->history ? ssb::next_pow2((int) std::max<int64_t>(4, 2 * r->history_ld)) : 0;
     sa.sel_slots = ssb::next_pow2(std::max(kb, 2));
     const int full_chunk = (int) div_up(r->vocab, 32) * 32;
-    const int occ = ssb::select_blocks_per_sm(kw, bf16, ssb::select_smem_bytes(kw, full_chunk, sa.hist_slots, sa.sel_slots));
+    const int occ = ssb::select_blocks_per_sm(kw, bf16, ssb::select_smem_bytes(kw, bf16, full_chunk, sa.hist_slots, sa.sel_slots));
     if (occ <= 0) return fail(SSB_DEVICE, "the selection kernel does not fit on this device");
     const int slots = std::min(kScratchSlots, d->sm_count * occ);
     const int min_chunk = all_greedy ? 2048 : 4096;

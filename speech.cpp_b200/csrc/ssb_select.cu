@@ -1,207 +1,48 @@
-// Large-vocabulary rows with top-k <= 128 (every drawing configuration of the Qwen3 text decoders and
-// the talker) and all-greedy batches: the HBM-bound hot path.
+// Large-vocabulary all-greedy batches (the Qwen3 text decoders' greedy steps, qwen3-decoder.cpp:422-437,
+// 492-510, and the host argmax of qwen3-asr/decoder.cpp:108-113): the first maximum of the restricted
+// logits (qwen3-tts/sampler.cpp:105-108), HBM-bound.
 //
 // One CTA streams `chunk` consecutive columns of one row (several CTAs per row when the batch is small;
-// the last to finish merges their results, as in ssb_stream.cu). Warp-specialized:
-//   producer warp  streams the chunk through a ring of kStages shared-memory stages with TMA bulk
-//                  copies (cp.async.bulk + mbarrier complete_tx), refilling a slot as soon as all
-//                  consumer warps have released it (an "empty" mbarrier per slot);
-//   8 consumers    reduce each stage with no block-wide synchronization:
-//     fast path, per 16-byte group: a NaN-propagating max (bf16x2 packed for bf16) folded into the
-//       restricted maximum (qwen3-tts/sampler.cpp:43-49) and one compare against the CTA's threshold.
-//       Groups holding a masked or history token, or reaching the threshold, are flagged.
-//     slow path: the flagged groups of a warp form a work list that its lanes take one each: widen,
-//       substitute -inf for masked tokens and the penalized value for history tokens, divide by the
-//       temperature exactly as the reference does (qwen3-tts/sampler.cpp:73), and key each element as a
-//       composite (value, then lowest index: the order of qwen3-tts/sampler.cpp:78-79 with
-//       haru/sampler.cpp:39's tie-break).
-//   greedy (KW = 0): the first maximum (qwen3-tts/sampler.cpp:105-108), kept as the CTA's largest
-//     composite by a shared 64-bit atomic max; a group is flagged when its maximum reaches its value.
-//   top-k (KW > 0): candidates (composites at or above the threshold) collect in a per-warp shared
-//     buffer; a full buffer is sorted by a bitonic network in registers and merged, under a lock with a
-//     bounded wait, into the CTA's shared queue of its best 32*KW composites. The threshold is the
-//     queue's k-th entry (plus one): every composite below it has k better ones already, so filtering
-//     on it is exact. The first stage seeds it with the k-th largest group maximum of each warp (k
-//     elements are at least that large; for a positive temperature, which keeps the logits' order).
-// Candidates are pre-tested on raw logits against raw_bound() so that the division runs only near the
-// top. The queue is the CTA's exact top-k, and finalize_draw replays the reference's double-precision
-// softmax, top-p cut and pick.
+// the last to finish merges their results, as in ssb_stream.cu). Warp-specialized: a producer warp
+// brings the chunk through a ring of kStages shared-memory stages with TMA bulk copies (cp.async.bulk +
+// mbarrier complete_tx), refilling a slot as soon as every consumer warp has copied its part into
+// registers. Each of 256 consumer lanes takes four 16-byte groups per stage:
+//   fast path: one NaN-propagating max over the lane's groups (packed bf16x2 for bf16), folded into the
+//     restricted maximum (qwen3-tts/sampler.cpp:43-49) and compared against the CTA's best value so
+//     far (a shared 64-bit composite atomic max). Groups that hold a masked or history token ("special"
+//     groups, marked in a per-group bitmap built before the stream) never take the fast path.
+//   slow path, for lanes whose maximum reaches the best and for special groups: widen, substitute
+//     -inf for masked tokens and the penalized logit for history tokens, and key each element as a
+//     composite (value, then lowest index) folded into the CTA's best.
+// The first stage seeds the threshold with the warps' largest lane maxima.
 #include <climits>
 #include <cuda_bf16.h>
 
 #include "ssb_device.cuh"
 #include "ssb_kernels.h"
+#include "ssb_tma.cuh"
 
 namespace ssb {
 
 namespace {
 
-constexpr int kStageBytes = 16384;
 constexpr int kStages = 3;
-constexpr int kConsumerWarps = 8;
-constexpr int kConsumers = kConsumerWarps * 32;
-constexpr int kThreads = kConsumers + 32;  // + the producer warp
-constexpr int kGroupsPerThread = kStageBytes / 16 / kConsumers;
-constexpr int kWarpBuf = 128;              // candidate buffer entries per consumer warp
-constexpr int kDefer = 64;                 // deferred flagged groups per consumer warp
-constexpr uint32_t kWaitLimit = 1u << 22;  // bounded mbarrier polls
-constexpr uint32_t kLockLimit = 1u << 22;  // bounded lock attempts
-
-static_assert(kGroupsPerThread * kConsumers * 16 == kStageBytes, "stage must split evenly");
-static_assert(kGroupsPerThread == 4, "the work list enumerates four groups per lane");
-
-__device__ __forceinline__ uint32_t smem_addr(const void * p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t * bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect(uint64_t * bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t * bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t * bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// Waits for phase `parity` of `bar`, giving up after kWaitLimit polls (returns false).
-__device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity) {
-    for (uint32_t n = 0; n < kWaitLimit; n++)
-        if (mbar_try_wait(bar, parity)) return true;
-    return false;
-}
-
-__device__ __forceinline__ void bulk_load(void * dst, const void * src, uint32_t bytes, uint64_t * bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_addr(dst)),
-                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
-                 : "memory");
-}
-
-template <typename TIn> __device__ __forceinline__ float group_max(const uint4 & r);
-template <> __device__ __forceinline__ float group_max<uint16_t>(const uint4 & r) {
-    const __nv_bfloat162 a = __hmax2_nan(*reinterpret_cast<const __nv_bfloat162 *>(&r.x),
-                                         *reinterpret_cast<const __nv_bfloat162 *>(&r.y));
-    const __nv_bfloat162 b = __hmax2_nan(*reinterpret_cast<const __nv_bfloat162 *>(&r.z),
-                                         *reinterpret_cast<const __nv_bfloat162 *>(&r.w));
-    const __nv_bfloat162 m = __hmax2_nan(a, b);
-    const uint32_t w = *reinterpret_cast<const uint32_t *>(&m);
-    return max_nan(bf16_lo(w), bf16_hi(w));
-}
-template <> __device__ __forceinline__ float group_max<float>(const uint4 & r) {
-    return max_nan(max_nan(__uint_as_float(r.x), __uint_as_float(r.y)), max_nan(__uint_as_float(r.z), __uint_as_float(r.w)));
-}
-
-// Multiplicative hash of a token id into `bits` bits (Knuth's multiplicative method).
-__device__ __forceinline__ uint32_t hash_token(int32_t t, int bits) { return ((uint32_t) t * 0x9E3779B1u) >> (32 - bits); }
-
-// Element i (= r * 32 + lane) of a warp-distributed array, for a warp-uniform i.
-template <int R>
-__device__ __forceinline__ uint64_t warp_get(const uint64_t (&x)[R], int i) {
-    uint64_t v = 0;
-#pragma unroll
-    for (int r = 0; r < R; r++)
-        if (r == (i >> 5)) v = x[r];
-    return __shfl_sync(0xffffffffu, v, i & 31);
-}
-
-// Merges the sorted (descending) 32*KW elements of `q` with the sorted 32*KW elements of `t`, keeping
-// the best 32*KW sorted in q: max against t reversed gives a bitonic sequence holding the best half,
-// which a bitonic clean-up sorts.
-template <int KW>
-__device__ __forceinline__ void warp_merge_sorted(uint64_t (&q)[KW], const uint64_t (&t)[KW]) {
-    const int lane = lane_id();
-#pragma unroll
-    for (int r = 0; r < KW; r++) {
-        const uint64_t o = __shfl_sync(0xffffffffu, t[KW - 1 - r], 31 - lane);
-        q[r] = q[r] > o ? q[r] : o;
-    }
-#pragma unroll
-    for (int j = 16 * KW; j > 0; j >>= 1) {
-#pragma unroll
-        for (int r = 0; r < KW; r++) {
-            if (j >= 32) {
-                const int rp = r ^ (j >> 5);
-                if (rp > r) {
-                    const uint64_t a = q[r], b = q[rp];
-                    if (a < b) q[r] = b, q[rp] = a;
-                }
-            } else {
-                const uint64_t o = shfl_xor(q[r], j);
-                const bool keep_max = (lane & j) == 0;
-                q[r] = keep_max ? (q[r] > o ? q[r] : o) : (q[r] < o ? q[r] : o);
-            }
-        }
-    }
-}
+constexpr int kGroupWordsPerStage = kConsumerWarps * kGroupsPerThread;  // special-group bitmap words per stage
+constexpr int kThreads = kStreamCtaThreads;
 
 // Shared state of the CTA's selection.
 struct Shared {
-    uint64_t theta;     // a candidate enters iff its composite >= theta (top-k)
-    uint64_t best;      // greedy: the largest composite seen
-    uint32_t seed_key;  // greedy: order key of the largest group maximum seen in a warp's first stage
-    int lock;
+    uint64_t best;      // the largest composite seen
+    uint32_t seed_key;  // order key of the largest lane maximum of a warp's first stage
     int abort;
 };
 
-// Sorts a warp's candidate buffer and merges its best into the CTA queue `gq` under the lock; raises
-// the threshold to the queue's k-th entry. Warp-wide; not inlined, so one copy of the networks exists.
-template <int QN, int R>
-__device__ __noinline__ void publish(const uint64_t * wbuf, int wn, uint64_t * gq, int k, Shared * sh) {
-    const int lane = lane_id();
-    uint64_t x[R];
-#pragma unroll
-    for (int r = 0; r < R; r++) {
-        const int i = r * 32 + lane;
-        x[r] = i < wn ? wbuf[i] : 0ull;
-    }
-    warp_sort_desc<R>(x);
-    uint64_t t[QN];
-#pragma unroll
-    for (int r = 0; r < QN; r++) t[r] = r < R ? x[r < R ? r : 0] : 0ull;
-    int got = 0;
-    if (lane == 0) {
-        for (uint32_t n = 0; n < kLockLimit; n++) {
-            if (atomicCAS(&sh->lock, 0, 1) == 0) {
-                got = 1;
-                break;
-            }
-        }
-    }
-    got = __shfl_sync(0xffffffffu, got, 0);
-    if (!got) {
-        if (lane == 0) sh->abort = 1;
-        return;
-    }
-    __threadfence_block();
-    uint64_t q[QN];
-#pragma unroll
-    for (int r = 0; r < QN; r++) q[r] = reinterpret_cast<volatile uint64_t *>(gq)[r * 32 + lane];
-    warp_merge_sorted<QN>(q, t);
-#pragma unroll
-    for (int r = 0; r < QN; r++) reinterpret_cast<volatile uint64_t *>(gq)[r * 32 + lane] = q[r];
-    const uint64_t kth = warp_get<QN>(q, k - 1);
-    __threadfence_block();
-    __syncwarp();
-    if (lane == 0) {
-        if (kth) atomicMax(reinterpret_cast<unsigned long long *>(&sh->theta), (unsigned long long) (kth + 1));
-        atomicExch(&sh->lock, 0);
-    }
-    __syncwarp();
+// Word of the special-group bitmap that holds group `gi` of the chunk (bit gi & 31): the four words of
+// one consumer warp in one stage are adjacent, so a warp reads them with one 16-byte load.
+__device__ __forceinline__ int group_word(int gi) {
+    const int st = gi / kStageGroups, within = gi - st * kStageGroups;
+    const int j = within / kConsumers, w = (within - j * kConsumers) >> 5;
+    return st * kGroupWordsPerStage + w * kGroupsPerThread + j;
 }
 
 struct Ctx {
@@ -211,7 +52,7 @@ struct Ctx {
     bool penal;
     const uint32_t * hbits;
     const int32_t * hkey;
-    const float * hval;
+    const int32_t * hcnt;
     int hbits_n;
     float tscale;
     bool fast;
@@ -219,13 +60,15 @@ struct Ctx {
     float * processed;
 };
 
-__device__ __forceinline__ float history_value(const Ctx & c, int32_t t) {
+// Occurrences of history token t in the row (t is in the table).
+__device__ __forceinline__ int history_count(const Ctx & c, int32_t t) {
     const uint32_t mask = (1u << c.hbits_n) - 1u;
     uint32_t h = hash_token(t, c.hbits_n);
     for (uint32_t n = 0; n <= mask && c.hkey[h] != t; n++) h = (h + 1) & mask;
-    return c.hval[h];
+    return c.hcnt[h];
 }
 
+// Masked (bits 0..G-1) and history (bits 16..16+G-1) columns among col0 .. col0+G-1.
 template <int G>
 __device__ __forceinline__ uint32_t special_bits(const Ctx & c, int col0) {
     uint32_t mb = 0, hb = 0;
@@ -238,19 +81,19 @@ __device__ __forceinline__ uint32_t special_bits(const Ctx & c, int col0) {
     return mb | (hb << 16);
 }
 
-// The restricted logit of column `col` whose raw value is x.
-__device__ __forceinline__ float restrict1(const Ctx & c, float x, int col, uint32_t sb, int e) {
+// The restricted logit of column `col` whose raw value is x: -inf where masked, the penalized logit
+// (qwen3-tts/sampler.cpp:36-38, then presence/frequency) for a history token, else x.
+__device__ __forceinline__ float restrict1(const Ctx & c, const RowParams & p, float x, int col, uint32_t sb, int e) {
     if ((sb >> e) & 1u) return -kInf;
-    if ((sb >> (16 + e)) & 1u) return history_value(c, col);
+    if ((sb >> (16 + e)) & 1u) return penalize(x, history_count(c, col), p);
     return x;
 }
 
-template <typename TIn, int KW, bool kDebug>
+template <typename TIn, bool kDebug>
 __global__ void __launch_bounds__(kThreads, 2) select_rows_kernel(const StreamArgs sa) {
     const RowsArgs & a = sa.r;
     constexpr int G = Elem<TIn>::kVec;
     constexpr int kStageElems = kStageBytes / (int) sizeof(TIn);
-    constexpr int QN = KW > 0 ? KW : 1;  // registers per lane of the CTA queue
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t s_full[kStages];
     __shared__ __align__(8) uint64_t s_empty[kStages];
@@ -268,55 +111,40 @@ __global__ void __launch_bounds__(kThreads, 2) select_rows_kernel(const StreamAr
     const int vocab = a.vocab;
     const ssb_params pp = a.row_params ? a.row_params[row] : a.params;
     const RowParams p = resolve_params(pp, vocab);
-    const bool greedy_row = KW == 0 || p.greedy;
-    const int k = greedy_row ? 1 : p.k;
-    if (KW > 0 && a.row_params && !p.greedy && p.k > a.k_bound) {
-        if (split == 0 && threadIdx.x == 0) {
-            a.ids[row] = -1, a.status[row] = SSB_ROW_INVALID_ROW;
-            if (kDebug && a.dbg_count) a.dbg_count[row] = 0;
-        }
-        return;
-    }
     const int c0 = split * sa.chunk;
     const int c1 = min(vocab, c0 + sa.chunk);
     const int len = c1 - c0;
-    const int nvec = len / G;
-    const int nstages = (nvec * 16 + kStageBytes - 1) / kStageBytes;
+    const int nvec = len / G;  // whole 16-byte groups; the rest are tail columns
+    const int nstages = (nvec + kStageGroups - 1) / kStageGroups;
 
-    // ---- shared memory: [ring] [history bitmap] [hash keys] [hash values] [warp buffers] [queue] [selected]
+    // ---- shared memory: [ring] [history bitmap] [special-group bitmap] [hash keys] [hash counts]
     unsigned char * ring = smem;
     const int hw_alloc = (((sa.chunk + 31) >> 5) + 3) & ~3;
+    const int gw_alloc = ((sa.chunk * (int) sizeof(TIn) + kStageBytes - 1) / kStageBytes) * kGroupWordsPerStage;
     uint32_t * s_hbits = reinterpret_cast<uint32_t *>(smem + kStages * kStageBytes);
-    int32_t * s_hkey = reinterpret_cast<int32_t *>(s_hbits + hw_alloc);
-    float * s_hval = reinterpret_cast<float *>(s_hkey + sa.hist_slots);
-    uint64_t * s_wbuf = reinterpret_cast<uint64_t *>(s_hval + sa.hist_slots);  // [kConsumerWarps][kWarpBuf]
-    uint64_t * s_queue = s_wbuf + kConsumerWarps * kWarpBuf;                    // [32*QN]
-    uint64_t * s_sel = s_queue + 32 * QN;                                      // [max(sel_slots, 32*QN)]
-    uint4 * s_draw = reinterpret_cast<uint4 *>(s_sel + (sa.sel_slots > 32 * QN ? sa.sel_slots : 32 * QN));  // [8][kDefer]
-    int * s_dcol = reinterpret_cast<int *>(s_draw + kConsumerWarps * kDefer);                               // [8][kDefer]
+    uint32_t * s_gbits = s_hbits + hw_alloc;
+    int32_t * s_hkey = reinterpret_cast<int32_t *>(s_gbits + gw_alloc);
+    int32_t * s_hcnt = s_hkey + sa.hist_slots;
 
     const TIn * src = reinterpret_cast<const TIn *>(a.logits) + (int64_t) row * a.ld;
     const char * gsrc = reinterpret_cast<const char *>(src + c0);
 
     if (threadIdx.x == 0) {
-        sh.theta = 0;
         sh.best = 0;
         sh.seed_key = 0;
-        sh.lock = 0;
         sh.abort = 0;
         for (int q = 0; q < kStages; q++) mbar_init(&s_full[q], 1), mbar_init(&s_empty[q], kConsumerWarps);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         for (int q = 0; q < kStages && q < nstages; q++) {
-            const uint32_t bytes = (uint32_t) min(kStageBytes, nvec * 16 - q * kStageBytes);
+            const uint32_t bytes = (uint32_t) min(kStageBytes, (nvec - q * kStageGroups) * 16);
             mbar_expect(&s_full[q], bytes);
             bulk_load(ring + q * kStageBytes, gsrc + (size_t) q * kStageBytes, bytes, &s_full[q]);
         }
     }
-    if (KW > 0)
-        for (int i = threadIdx.x; i < 32 * QN; i += blockDim.x) s_queue[i] = 0;
 
-    // ---- history: hash table of the distinct in-range ids (duplicates combined per warp first)
+    // ---- special groups: history tokens (hash table of distinct ids with their counts, per-column
+    //      bitmap) and masked tokens, marked per 16-byte group for the fast path
     const int32_t * hist = a.history ? a.history + (int64_t) row * a.history_ld : nullptr;
     int hlen = 0;
     if (hist) {
@@ -324,39 +152,78 @@ __global__ void __launch_bounds__(kThreads, 2) select_rows_kernel(const StreamAr
         hlen = hlen < 0 ? 0 : (hlen > (int) a.history_ld ? (int) a.history_ld : hlen);
     }
     const bool penal = p.history_applies && hlen > 0;
+    const uint32_t * mrow = (a.mask && a.mask_kind != SSB_MASK_NONE) ? a.mask + (int64_t) row * a.mask_ld : nullptr;
+    const bool special = mrow != nullptr || penal;
     const int hbits_n = sa.hist_slots > 1 ? 31 - __clz(sa.hist_slots) : 1;
-    if (penal) {
-        const int nw = (sa.chunk + 31) >> 5;
-        for (int i = threadIdx.x; i < nw; i += blockDim.x) s_hbits[i] = 0;
-        for (int i = threadIdx.x; i < sa.hist_slots; i += blockDim.x) s_hkey[i] = -1, s_hval[i] = 0.0f;
+    if (special) {
+        for (int i = threadIdx.x; i < nstages * kGroupWordsPerStage; i += blockDim.x) s_gbits[i] = 0;
+        if (penal) {
+            const int nw = (sa.chunk + 31) >> 5;
+            for (int i = threadIdx.x; i < nw; i += blockDim.x) s_hbits[i] = 0;
+            for (int i = threadIdx.x; i < sa.hist_slots; i += blockDim.x) s_hkey[i] = -1, s_hcnt[i] = 0;
+        }
         __syncthreads();
-        const uint32_t hmask = (uint32_t) sa.hist_slots - 1u;
-        for (int base = 0; base < hlen; base += blockDim.x) {  // warp-uniform trip count
-            const int i = base + (int) threadIdx.x;
-            const int32_t t = i < hlen ? hist[i] : -1;
-            const bool in = t >= c0 && t < c1;
-            const unsigned m = __ballot_sync(0xffffffffu, in);
-            if (in) {
-                const unsigned peers = __match_any_sync(m, t);
-                if (lane == __ffs(peers) - 1) {
-                    uint32_t h = hash_token(t, hbits_n);
-                    for (uint32_t n = 0; n <= hmask; n++) {
-                        const int32_t old = atomicCAS(&s_hkey[h], -1, t);
-                        if (old == -1 || old == t) {
-                            atomicAdd(&s_hval[h], (float) __popc(peers));  // counts, exact below 2^24
-                            break;
+        if (penal) {
+            const uint32_t hmask = (uint32_t) sa.hist_slots - 1u;
+            for (int base = 0; base < hlen; base += 4 * kThreads) {  // warp-uniform trip count
+                int32_t t[4];
+#pragma unroll
+                for (int q = 0; q < 4; q++) {  // four independent loads in flight
+                    const int i = base + q * kThreads + (int) threadIdx.x;
+                    t[q] = i < hlen ? __ldg(hist + i) : -1;
+                }
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const bool in = t[q] >= c0 && t[q] < c1;
+                    const unsigned m = __ballot_sync(0xffffffffu, in);
+                    if (in) {
+                        const unsigned peers = __match_any_sync(m, t[q]);  // duplicates within the warp
+                        if (lane == __ffs(peers) - 1) {
+                            uint32_t h = hash_token(t[q], hbits_n);
+                            for (uint32_t n = 0; n <= hmask; n++) {
+                                const int32_t old = atomicCAS(&s_hkey[h], -1, t[q]);
+                                if (old == -1 || old == t[q]) {
+                                    atomicAdd(&s_hcnt[h], __popc(peers));
+                                    break;
+                                }
+                                h = (h + 1) & hmask;
+                            }
+                            const int rel = t[q] - c0;
+                            atomicOr(&s_hbits[rel >> 5], 1u << (rel & 31));
+                            const int gi = rel / G;
+                            if (gi < nvec) atomicOr(&s_gbits[group_word(gi)], 1u << (gi & 31));
                         }
-                        h = (h + 1) & hmask;
                     }
                 }
             }
         }
-        __syncthreads();
-        for (int i = threadIdx.x; i < sa.hist_slots; i += blockDim.x) {
-            const int32_t t = s_hkey[i];
-            if (t >= 0) {
-                s_hval[i] = penalize(Elem<TIn>::load1(src, t), (int) s_hval[i], p);
-                atomicOr(&s_hbits[(t - c0) >> 5], 1u << ((t - c0) & 31));
+        if (mrow) {
+            // one mask word covers 32/G whole groups (c0 is a multiple of 32)
+            constexpr int kGroupsPerWord = 32 / G;
+            constexpr uint32_t gfull = (1u << G) - 1u;
+            const int w0 = c0 >> 5, nw = (len + 31) >> 5;
+            for (int base = 0; base < nw; base += 4 * kThreads) {
+                uint32_t mw[4];
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const int i = base + q * kThreads + (int) threadIdx.x;
+                    mw[q] = i < nw ? __ldg(mrow + w0 + i) : 0u;
+                }
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const int i = base + q * kThreads + (int) threadIdx.x;
+                    const int gi0 = i * kGroupsPerWord;
+                    if (i < nw && gi0 < nvec) {
+                        uint32_t sb = 0;
+#pragma unroll
+                        for (int gg = 0; gg < kGroupsPerWord; gg++) {
+                            const uint32_t bits = (mw[q] >> (gg * G)) & gfull;
+                            sb |= (uint32_t) (a.mask_kind == SSB_MASK_BAN ? bits != 0u : bits != gfull) << gg;
+                        }
+                        if (gi0 + kGroupsPerWord > nvec) sb &= (1u << (nvec - gi0)) - 1u;
+                        if (sb) atomicOr(&s_gbits[group_word(gi0)], sb << (gi0 & 31));
+                    }
+                }
             }
         }
     }
@@ -365,101 +232,56 @@ __global__ void __launch_bounds__(kThreads, 2) select_rows_kernel(const StreamAr
     Ctx c;
     c.c0 = c0;
     c.mask_kind = a.mask_kind;
-    c.mrow = (a.mask && a.mask_kind != SSB_MASK_NONE) ? a.mask + (int64_t) row * a.mask_ld : nullptr;
+    c.mrow = mrow;
     c.penal = penal;
     c.hbits = s_hbits;
     c.hkey = s_hkey;
-    c.hval = s_hval;
+    c.hcnt = s_hcnt;
     c.hbits_n = hbits_n;
-    c.scale = !greedy_row;
-    c.tscale = greedy_row ? 1.0f : p.temperature;
-    c.fast = greedy_row ? true : p.fast_scale;
     c.processed = (kDebug && a.dbg_processed) ? a.dbg_processed + (int64_t) row * vocab : nullptr;
-    const bool special = c.mrow != nullptr || penal;
 
     float acc = -kInf;
-    int nan_scaled = 0;
-    uint64_t theta = 0;   // top-k: composites below it cannot be among the k best; greedy: the best so far
-    float thr = -kInf;    // raw logits below thr cannot reach theta
-    uint64_t * wbuf = s_wbuf + warp * kWarpBuf;
-    int wn = 0;           // warp-uniform count of wbuf
+    uint64_t theta = 0;  // the best composite so far
+    float thr = -kInf;   // raw logits below thr cannot reach theta
 
-    // refreshes theta/thr from the shared state
+    // raises theta/thr to the shared state
     auto refresh = [&]() {
-        const uint64_t t = *reinterpret_cast<volatile uint64_t *>(KW > 0 ? &sh.theta : &sh.best);
+        const uint64_t t = *reinterpret_cast<volatile uint64_t *>(&sh.best);
         if (t > theta) {
             theta = t;
-            const float b = KW > 0 ? raw_bound(composite_value(theta), c.tscale, c.fast) : composite_value(theta);
+            const float b = composite_value(theta);
             thr = b > thr ? b : thr;
         }
-        if (KW == 0) {
-            const uint32_t sk = *reinterpret_cast<volatile uint32_t *>(&sh.seed_key);
-            if (sk) {
-                const float b = key_value(sk);
-                thr = b > thr ? b : thr;
-            }
+        const uint32_t sk = *reinterpret_cast<volatile uint32_t *>(&sh.seed_key);
+        if (sk) {
+            const float b = key_value(sk);
+            thr = b > thr ? b : thr;
         }
     };
-    // merges the warp's buffered candidates into the CTA queue (sorting only as many as it holds)
-    auto flush = [&]() {
-        __syncwarp();
-        if (wn <= 32) publish<QN, 1>(wbuf, wn, s_queue, k, &sh);
-        else if (wn <= 64) publish<QN, 2>(wbuf, wn, s_queue, k, &sh);
-        else publish<QN, 4>(wbuf, wn, s_queue, k, &sh);
-        wn = 0;
-        refresh();
-    };
-    // appends each lane's candidate `cv` (where `has`) to the warp buffer; flushes when it could overflow
-    auto append = [&](bool has, uint64_t cv) {
-        const unsigned m = __ballot_sync(0xffffffffu, has);
-        if (!m) return;
-        if (has) wbuf[wn + __popc(m & ((1u << lane) - 1u))] = cv;
-        wn += __popc(m);
-        if (wn > kWarpBuf - 32) flush();
-    };
-    // top-k: the per-element test of a candidate (restricted value v at column col), warp-uniform
-    auto element = [&](bool valid, float v, int col) {
-        bool has = false;
-        uint64_t cv = 0;
-        if (valid && v >= thr) {
-            const float sc = c.scale ? __fdiv_rn(v, c.tscale) : v;
-            nan_scaled |= sc != sc;
-            cv = composite(sc, (uint32_t) col);
-            has = cv >= theta;
-        }
-        append(has, cv);
-    };
-    // one flagged group per lane (has): widen, restrict, fold into the statistics, test its elements
+    // one flagged group per lane (has): widen, restrict, fold into the statistics; the lane's best
     auto process_item = [&](bool has, const uint4 & raw, int col0) {
         float v[G];
         uint32_t sb = 0;
         if (has) {
             Elem<TIn>::unpack(raw, v);
             sb = special ? special_bits<G>(c, col0) : 0u;
-        } else {
-#pragma unroll
-            for (int e = 0; e < G; e++) v[e] = -kInf;
         }
         uint64_t lbest = 0;
 #pragma unroll
         for (int e = 0; e < G; e++) {
             if (has) {
-                v[e] = restrict1(c, v[e], col0 + e, sb, e);
+                if (special) v[e] = restrict1(c, p, v[e], col0 + e, sb, e);
                 acc = max_nan(acc, v[e]);
                 if (kDebug && c.processed) c.processed[col0 + e] = v[e];
-            }
-            if (KW == 0) {
-                if (has && v[e] == v[e] && v[e] >= thr) {
+                if (v[e] == v[e] && v[e] >= thr) {
                     const uint64_t cv = composite(v[e], (uint32_t) (col0 + e));
                     lbest = cv > lbest ? cv : lbest;
                 }
-            } else {
-                element(has, v[e], col0 + e);
             }
         }
         return lbest;
     };
-    // greedy: folds each lane's best composite of an item into the CTA's best, once per warp
+    // folds each lane's best composite of an item into the CTA's best, once per warp
     auto greedy_fold = [&](uint64_t lbest) {
         const uint64_t m = warp_max_u64(lbest);
         if (m > theta) {
@@ -470,29 +292,12 @@ __global__ void __launch_bounds__(kThreads, 2) select_rows_kernel(const StreamAr
         }
     };
 
-    // the deferred flagged groups of this warp, 32 per pass; then the candidates reach the CTA queue
-    int dn = 0;  // warp-uniform count of deferred groups
-    auto process_deferred = [&]() {
-        __syncwarp();
-        for (int base = 0; base < dn; base += 32) {  // warp-uniform
-            const int item = base + lane;
-            const bool has = item < dn;
-            const uint4 raw = has ? s_draw[warp * kDefer + item] : make_uint4(0, 0, 0, 0);
-            const int col0 = has ? s_dcol[warp * kDefer + item] : c0;
-            process_item(has, raw, col0);
-        }
-        dn = 0;
-        if (wn >= 32) flush();
-        __syncwarp();
-    };
-    auto consumer_sync = [&]() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory"); };
-
     if (producer) {
         if (lane == 0) {
             for (int st = kStages; st < nstages; st++) {
                 const int slot = st % kStages;
                 if (!mbar_wait(&s_empty[slot], (uint32_t) ((st / kStages) - 1) & 1u)) sh.abort = 1;
-                const uint32_t bytes = (uint32_t) min(kStageBytes, nvec * 16 - st * kStageBytes);
+                const uint32_t bytes = (uint32_t) min(kStageBytes, (nvec - st * kStageGroups) * 16);
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 mbar_expect(&s_full[slot], bytes);
                 bulk_load(ring + slot * kStageBytes, gsrc + (size_t) st * kStageBytes, bytes, &s_full[slot]);
@@ -500,131 +305,79 @@ __global__ void __launch_bounds__(kThreads, 2) select_rows_kernel(const StreamAr
         }
     } else {
         const int tid = (int) threadIdx.x;  // 0 .. kConsumers-1
+        const uint4 * gb4 = reinterpret_cast<const uint4 *>(s_gbits);
+        int slot = 0;
+        uint32_t phase = 0;
         for (int st = 0; st < nstages; st++) {
-            const int slot = st % kStages;
             const uint4 * stage = reinterpret_cast<const uint4 *>(ring + slot * kStageBytes);
-            if (!mbar_wait(&s_full[slot], (uint32_t) (st / kStages) & 1u)) sh.abort = 1;
-            refresh();
-            const int sbase = c0 + st * kStageElems;
-            const int sgroups = min(kStageBytes, nvec * 16 - st * kStageBytes) / 16;
-            // fast path
-            uint32_t flagged = 0;
-            float gmax[kGroupsPerThread];
+            if (!mbar_wait(&s_full[slot], phase)) sh.abort = 1;
+            const int sgroups = min(kStageGroups, nvec - st * kStageGroups);
+            uint4 rv[kGroupsPerThread];
+            uint32_t live = 0;
 #pragma unroll
             for (int j = 0; j < kGroupsPerThread; j++) {
                 const int g = j * kConsumers + tid;
-                gmax[j] = -kInf;
-                if (g >= sgroups) continue;
-                bool flag = kDebug || (special && special_bits<G>(c, sbase + g * G) != 0);
-                if (!flag) {
-                    const float gm = group_max<TIn>(stage[g]);
-                    gmax[j] = gm;
-                    acc = max_nan(acc, gm);
-                    flag = gm >= thr;
+                if (g < sgroups) {
+                    rv[j] = stage[g];
+                    live |= 1u << j;
+                } else {
+                    rv[j] = neg_inf_group<TIn>();
                 }
-                flagged |= (uint32_t) flag << j;
             }
-            // greedy: the warp's largest group maximum of the first stage is a value the maximum reaches
-            if (KW == 0 && st == 0) {
-                float wm = -kInf;
+            uint32_t sp = 0;
+            if (special) {
+                const uint4 gw = gb4[st * kConsumerWarps + warp];
+                sp = (((gw.x >> lane) & 1u) | (((gw.y >> lane) & 1u) << 1) | (((gw.z >> lane) & 1u) << 2) |
+                      (((gw.w >> lane) & 1u) << 3)) & live;
+            }
+            // the lane's part of the stage is in registers: release the slot to the producer
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_empty[slot]);
+            if (++slot == kStages) slot = 0, phase ^= 1u;
+            refresh();
+            const int sbase = c0 + st * kStageElems;
+            const uint32_t plain = live & ~sp;  // groups whose raw values are their restricted values
+            float lm;
+            if (plain == 0xFu) {
+                lm = lane_max<TIn>(rv);
+            } else {
+                lm = -kInf;
 #pragma unroll
                 for (int j = 0; j < kGroupsPerThread; j++)
-                    if (gmax[j] == gmax[j] && gmax[j] > wm) wm = gmax[j];
+                    if ((plain >> j) & 1u) lm = max_nan(lm, group_max<TIn>(rv[j]));
+            }
+            acc = max_nan(acc, lm);
+            if (st == 0) {
+                // the warp's largest lane maximum is a value the row's maximum reaches
+                float wm = lm == lm ? lm : -kInf;
 #pragma unroll
                 for (int o = 16; o; o >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, o));
                 if (wm > thr) {
                     if (lane == 0) atomicMax(&sh.seed_key, order_key(wm));
                     thr = wm;
-                    flagged = 0;
-#pragma unroll
-                    for (int j = 0; j < kGroupsPerThread; j++) {
-                        const int g = j * kConsumers + tid;
-                        if (g < sgroups)
-                            flagged |= (uint32_t) (kDebug || gmax[j] >= thr || gmax[j] != gmax[j] ||
-                                                   (special && special_bits<G>(c, sbase + g * G) != 0))
-                                       << j;
-                    }
                 }
             }
-            // top-k: the first stage seeds the CTA's threshold with the k-th largest of its group maxima
-            // (k elements are at least that large; a positive temperature keeps the logits' order)
-            if (KW > 0 && st == 0 && c.fast) {
-                uint64_t seeds[kGroupsPerThread];
+            const bool hit = kDebug ? live != 0u : (sp != 0u || lm >= thr);
+            if (__any_sync(0xffffffffu, hit)) {
+                uint32_t fl = 0;
+                if (hit) {
+                    if (kDebug) {
+                        fl = live;
+                    } else {
+                        fl = sp;
+                        if (lm >= thr) {
+#pragma unroll
+                            for (int j = 0; j < kGroupsPerThread; j++)
+                                if (((plain >> j) & 1u) && group_max<TIn>(rv[j]) >= thr) fl |= 1u << j;
+                        }
+                    }
+                }
 #pragma unroll
                 for (int j = 0; j < kGroupsPerThread; j++)
-                    seeds[j] = (uint64_t) order_key(gmax[j] == gmax[j] ? gmax[j] : -kInf) << 32;
-                warp_sort_desc<kGroupsPerThread>(seeds);
-#pragma unroll
-                for (int r = 0; r < QN; r++) s_wbuf[warp * kWarpBuf + r * 32 + lane] = seeds[r];
-                consumer_sync();
-                if (warp == 0) {
-                    uint64_t q[QN];
-#pragma unroll
-                    for (int r = 0; r < QN; r++) q[r] = s_wbuf[r * 32 + lane];
-                    for (int w = 1; w < kConsumerWarps; w++) {
-                        uint64_t t[QN];
-#pragma unroll
-                        for (int r = 0; r < QN; r++) t[r] = s_wbuf[w * kWarpBuf + r * 32 + lane];
-                        warp_merge_sorted<QN>(q, t);
-                    }
-                    const float s0raw = composite_value(warp_get<QN>(q, k - 1));
-                    if (lane == 0 && s0raw > -kInf) {
-                        const float s0 = c.scale ? __fdiv_rn(s0raw, c.tscale) : s0raw;
-                        atomicMax(reinterpret_cast<unsigned long long *>(&sh.theta), (unsigned long long) order_key(s0) << 32);
-                    }
-                }
-                consumer_sync();
-                refresh();
-                flagged = 0;
-#pragma unroll
-                for (int j = 0; j < kGroupsPerThread; j++) {
-                    const int g = j * kConsumers + tid;
-                    if (g < sgroups)
-                        flagged |= (uint32_t) (kDebug || gmax[j] >= thr || gmax[j] != gmax[j] ||
-                                               (special && special_bits<G>(c, sbase + g * G) != 0))
-                                   << j;
-                }
+                    if (__any_sync(0xffffffffu, (fl >> j) & 1u))
+                        greedy_fold(process_item((fl >> j) & 1u, rv[j], sbase + (j * kConsumers + tid) * G));
             }
-            // the warp's flagged groups
-            unsigned bl[kGroupsPerThread];
-            int total = 0;
-#pragma unroll
-            for (int j = 0; j < kGroupsPerThread; j++) bl[j] = __ballot_sync(0xffffffffu, (flagged >> j) & 1u), total += __popc(bl[j]);
-            if (KW > 0 && total > 0 && dn + total > kDefer) process_deferred();
-            if (KW > 0 && total > 0 && total <= kDefer) {
-                // top-k: defer them (raw bytes and column) and take them 32 at a time
-                int off = 0;
-#pragma unroll
-                for (int j = 0; j < kGroupsPerThread; j++) {
-                    if ((flagged >> j) & 1u) {
-                        const int pos = dn + off + __popc(bl[j] & ((1u << lane) - 1u));
-                        const int g = j * kConsumers + tid;
-                        s_draw[warp * kDefer + pos] = stage[g];
-                        s_dcol[warp * kDefer + pos] = sbase + g * G;
-                    }
-                    off += __popc(bl[j]);
-                }
-                dn += total;
-                if (dn >= 32) process_deferred();
-            } else {
-                // greedy, or a flood larger than the deferred list: the groups straight from the stage
-                for (int base = 0; base < total; base += 32) {  // warp-uniform
-                    const int item = base + lane;
-                    const bool has = item < total;
-                    int jj = 0, r = item;
-                    const int n0 = __popc(bl[0]), n1 = __popc(bl[1]), n2 = __popc(bl[2]);
-                    if (r >= n0) { r -= n0; jj = 1; if (r >= n1) { r -= n1; jj = 2; if (r >= n2) { r -= n2; jj = 3; } } }
-                    const unsigned bj = jj == 0 ? bl[0] : (jj == 1 ? bl[1] : (jj == 2 ? bl[2] : bl[3]));
-                    const int srcl = has ? (int) __fns(bj, 0, r + 1) : 0;
-                    const int g = jj * kConsumers + warp * 32 + srcl;
-                    const uint64_t lbest = process_item(has, has ? stage[g] : make_uint4(0, 0, 0, 0), sbase + g * G);
-                    if (KW == 0) greedy_fold(lbest);
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_empty[slot]);
         }
-        if (KW > 0 && dn > 0) process_deferred();
         // columns past the last whole 16-byte group: one per lane
         for (int base = c0 + nvec * G; base < c1; base += kConsumers) {  // warp-uniform trip count
             const int col = base + tid;
@@ -632,44 +385,29 @@ __global__ void __launch_bounds__(kThreads, 2) select_rows_kernel(const StreamAr
             float v = -kInf;
             if (ok) {
                 v = Elem<TIn>::load1(src, col);
-                if (special) v = restrict1(c, v, col, special_bits<1>(c, col), 0);
+                if (special) v = restrict1(c, p, v, col, special_bits<1>(c, col), 0);
                 acc = max_nan(acc, v);
                 if (kDebug && c.processed) c.processed[col] = v;
             }
             refresh();
-            if (KW == 0) greedy_fold(ok && v == v && v >= thr ? composite(v, (uint32_t) col) : 0ull);
-            else element(ok, v, col);
+            greedy_fold(ok && v == v && v >= thr ? composite(v, (uint32_t) col) : 0ull);
         }
-        if (KW > 0 && wn > 0) flush();
-        if (KW == 0 && lane == 0)
-            atomicMax(reinterpret_cast<unsigned long long *>(&sh.best), (unsigned long long) theta);
+        if (lane == 0) atomicMax(reinterpret_cast<unsigned long long *>(&sh.best), (unsigned long long) theta);
     }
 
     // ---- this CTA's result
     __syncthreads();
     const float rmax = block_max_nan(acc, s_redf);
-    const int nanf = block_or(nan_scaled, s_redi) | (sh.abort ? 2 : 0);
+    const int nanf = sh.abort ? 2 : 0;
     uint64_t best = sh.best;
-    int kk = 1;
-    if (KW > 0) {
-        for (int i = threadIdx.x; i < 32 * QN; i += blockDim.x) s_sel[i] = s_queue[i];
-        __syncthreads();
-        int nz = 0;
-        for (int i = 0; i < 32 * QN && s_sel[i] != 0; i++) nz++;
-        kk = nz < k ? nz : k;
-    }
 
     float row_max = rmax;
     int row_flags = nanf;
     if (splits > 1) {
         const int64_t slot = (int64_t) row * splits + split;
-        if (KW == 0) {
-            if (threadIdx.x == 0) sa.part_cand[slot * sa.r.k_bound] = best;
-        } else {
-            for (int i = threadIdx.x; i < kk; i += blockDim.x) sa.part_cand[slot * sa.r.k_bound + i] = s_sel[i];
-        }
         if (threadIdx.x == 0) {
-            sa.part_n[slot] = kk;
+            sa.part_cand[slot * sa.r.k_bound] = best;
+            sa.part_n[slot] = 1;
             sa.part_max[slot] = rmax;
             sa.part_flags[slot] = nanf;
         }
@@ -682,110 +420,44 @@ __global__ void __launch_bounds__(kThreads, 2) select_rows_kernel(const StreamAr
         if (threadIdx.x == 0) sa.counters[row] = 0;  // ready for the next launch
         float m = -kInf;
         int f = 0;
+        uint64_t b = 0;
         for (int q = threadIdx.x; q < splits; q += blockDim.x) {
             m = max_nan(m, __ldcg(sa.part_max + (int64_t) row * splits + q));
             f |= __ldcg(sa.part_flags + (int64_t) row * splits + q);
+            const uint64_t cv = __ldcg(reinterpret_cast<const unsigned long long *>(sa.part_cand) +
+                                       ((int64_t) row * splits + q) * sa.r.k_bound);
+            b = cv > b ? cv : b;
         }
         row_max = block_max_nan(m, s_redf);
-        row_flags = block_or(f & 1, s_redi) | (block_or(f & 2, s_redi) ? 2 : 0);
-        if (KW == 0) {
-            uint64_t b = 0;
-            for (int q = threadIdx.x; q < splits; q += blockDim.x) {
-                const uint64_t cv = __ldcg(reinterpret_cast<const unsigned long long *>(sa.part_cand) +
-                                           ((int64_t) row * splits + q) * sa.r.k_bound);
-                b = cv > b ? cv : b;
-            }
-            best = block_max_u64(b, s_red64);
-        } else {
-            // each consumer warp merges the lists of splits w, w+8, ...; warp 0 merges the warps' results
-            if (warp < kConsumerWarps) {
-                uint64_t q[QN];
-#pragma unroll
-                for (int r = 0; r < QN; r++) q[r] = 0;
-                for (int sp = warp; sp < splits; sp += kConsumerWarps) {
-                    const int64_t sl = (int64_t) row * splits + sp;
-                    const int n = __ldcg(sa.part_n + sl);
-                    uint64_t t[QN];
-#pragma unroll
-                    for (int r = 0; r < QN; r++) {
-                        const int i = r * 32 + lane;
-                        t[r] = i < n ? __ldcg(reinterpret_cast<const unsigned long long *>(sa.part_cand) + sl * sa.r.k_bound + i)
-                                     : 0ull;
-                    }
-                    warp_merge_sorted<QN>(q, t);
-                }
-#pragma unroll
-                for (int r = 0; r < QN; r++) s_wbuf[warp * kWarpBuf + r * 32 + lane] = q[r];
-            }
-            __syncthreads();
-            if (warp == 0) {
-                uint64_t q[QN];
-#pragma unroll
-                for (int r = 0; r < QN; r++) q[r] = s_wbuf[r * 32 + lane];
-                for (int w = 1; w < kConsumerWarps; w++) {
-                    uint64_t t[QN];
-#pragma unroll
-                    for (int r = 0; r < QN; r++) t[r] = s_wbuf[w * kWarpBuf + r * 32 + lane];
-                    warp_merge_sorted<QN>(q, t);
-                }
-#pragma unroll
-                for (int r = 0; r < QN; r++) s_sel[r * 32 + lane] = q[r];
-            }
-            __syncthreads();
-            int nz = 0;
-            for (int i = 0; i < 32 * QN && s_sel[i] != 0; i++) nz++;
-            kk = nz < k ? nz : k;
-        }
+        row_flags = block_or(f & 2, s_redi) ? 2 : 0;
+        best = block_max_u64(b, s_red64);
     }
 
     // ---- finalize the row (one CTA)
     int32_t * id_out = a.ids + row;
     int32_t * st_out = a.status + row;
-    RowOut out{id_out, st_out, nullptr, nullptr, nullptr, 0};
-    if (kDebug) {
-        out.tokens = a.dbg_tokens ? a.dbg_tokens + (int64_t) row * a.dbg_cap : nullptr;
-        out.weights = a.dbg_weights ? a.dbg_weights + (int64_t) row * a.dbg_cap : nullptr;
-        out.count = a.dbg_count ? a.dbg_count + row : nullptr;
-        out.cap = a.dbg_cap;
-    }
-    int stt = (row_flags & 2) ? SSB_ROW_DEVICE_TIMEOUT : restricted_status(row_max, p.rep);
-    if (stt == SSB_ROW_OK && !greedy_row && (row_flags & 1)) stt = SSB_ROW_TEMPERATURE_OVERFLOW;
-    if (stt != SSB_ROW_OK) {
-        if (threadIdx.x == 0) {
-            *id_out = -1, *st_out = stt;
-            if (out.count) *out.count = 0;
+    const int stt = (row_flags & 2) ? SSB_ROW_DEVICE_TIMEOUT : restricted_status(row_max, p.rep);
+    if (threadIdx.x == 0) {
+        const int32_t id = stt == SSB_ROW_OK ? (int32_t) composite_index(best) : -1;
+        *id_out = id, *st_out = stt;
+        if (kDebug) {
+            if (a.dbg_count) a.dbg_count[row] = stt == SSB_ROW_OK ? 1 : 0;
+            if (stt == SSB_ROW_OK && a.dbg_tokens && a.dbg_cap > 0) {
+                a.dbg_tokens[(int64_t) row * a.dbg_cap] = id;
+                a.dbg_weights[(int64_t) row * a.dbg_cap] = 1.0;
+            }
         }
-        return;
     }
-    if (greedy_row) {
-        if (KW > 0) best = s_sel[0];
-        if (threadIdx.x == 0) {
-            *id_out = (int32_t) composite_index(best), *st_out = SSB_ROW_OK;
-            if (out.count) *out.count = 1;
-            if (out.tokens && out.cap > 0) out.tokens[0] = *id_out, out.weights[0] = 1.0;
-        }
-        return;
-    }
-    const double u = a.u ? a.u[row] : 0.0;
-    finalize_draw(s_sel, kk, p, u, reinterpret_cast<double *>(s_wbuf), out);
 }
 
-template <typename TIn, int KW, bool kDebug>
+template <typename TIn, bool kDebug>
 void * kernel_ptr() {
-    return reinterpret_cast<void *>(select_rows_kernel<TIn, KW, kDebug>);
+    return reinterpret_cast<void *>(select_rows_kernel<TIn, kDebug>);
 }
 
-void * pick_kernel(int kw, bool bf16, bool debug) {
-#define SSB_KW(T)                                                                                       \
-    switch (kw) {                                                                                      \
-        case 0: return debug ? kernel_ptr<T, 0, true>() : kernel_ptr<T, 0, false>();                   \
-        case 1: return debug ? kernel_ptr<T, 1, true>() : kernel_ptr<T, 1, false>();                   \
-        case 2: return debug ? kernel_ptr<T, 2, true>() : kernel_ptr<T, 2, false>();                   \
-        default: return debug ? kernel_ptr<T, 4, true>() : kernel_ptr<T, 4, false>();                  \
-    }
-    if (bf16) SSB_KW(uint16_t)
-    SSB_KW(float)
-#undef SSB_KW
+void * pick_kernel(bool bf16, bool debug) {
+    if (bf16) return debug ? kernel_ptr<uint16_t, true>() : kernel_ptr<uint16_t, false>();
+    return debug ? kernel_ptr<float, true>() : kernel_ptr<float, false>();
 }
 
 }  // namespace
@@ -795,16 +467,17 @@ int select_kw(int k_bound, bool all_greedy) {
     return k_bound <= 32 ? 1 : (k_bound <= 64 ? 2 : 4);
 }
 
-size_t select_smem_bytes(int kw, int chunk, int hist_slots, int sel_slots) {
+size_t select_smem_bytes(int kw, bool bf16, int chunk, int hist_slots, int sel_slots) {
+    if (kw > 0) return topk_smem_bytes(kw, bf16, chunk, hist_slots, sel_slots);
     const size_t hwords = (size_t) ((((chunk + 31) >> 5) + 3) & ~3);
-    const int qn = kw > 0 ? kw : 1;
-    return (size_t) kStages * kStageBytes + hwords * 4 + (size_t) hist_slots * 8 +
-           (size_t) kConsumerWarps * kWarpBuf * 8 + (size_t) 32 * qn * 8 +
-           (size_t) (sel_slots > 32 * qn ? sel_slots : 32 * qn) * 8 + (size_t) kConsumerWarps * kDefer * (16 + 4);
+    const int64_t chunk_bytes = (int64_t) chunk * (bf16 ? 2 : 4);
+    const size_t gwords = (size_t) ((chunk_bytes + kStageBytes - 1) / kStageBytes) * kGroupWordsPerStage;
+    return (size_t) kStages * kStageBytes + hwords * 4 + gwords * 4 + (size_t) hist_slots * 8;
 }
 
 int select_blocks_per_sm(int kw, bool bf16, size_t smem) {
-    void * kern = pick_kernel(kw, bf16, false);
+    if (kw > 0) return topk_blocks_per_sm(kw, bf16, smem);
+    void * kern = pick_kernel(bf16, false);
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem) != cudaSuccess) return 0;
     int n = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, smem) != cudaSuccess) return 0;
@@ -812,8 +485,9 @@ int select_blocks_per_sm(int kw, bool bf16, size_t smem) {
 }
 
 cudaError_t launch_select(const StreamArgs & a, int kw, bool bf16, bool debug, cudaStream_t stream) {
-    const size_t smem = select_smem_bytes(kw, a.chunk, a.hist_slots, a.sel_slots);
-    void * kern = pick_kernel(kw, bf16, debug);
+    if (kw > 0) return launch_topk(a, kw, bf16, debug, stream);
+    const size_t smem = select_smem_bytes(0, bf16, a.chunk, a.hist_slots, a.sel_slots);
+    void * kern = pick_kernel(bf16, debug);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
     if (e != cudaSuccess) return e;
     void * args[] = {const_cast<StreamArgs *>(&a)};
