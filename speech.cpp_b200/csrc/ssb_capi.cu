@@ -17,6 +17,7 @@
 struct ssb_context {
     int device = 0;
     int sm_count = 0;
+    int max_smem = 0;   // opt-in shared memory per block
     int max_slots = 0;  // resident CTAs of the streaming kernel the scratch is sized for
     // split-row scratch, sized once at creation (rows * splits never exceeds max_slots)
     uint64_t * part_cand = nullptr;  // [max_slots * kStreamMaxK]
@@ -32,6 +33,7 @@ struct ssb_context {
     int occupancy[2][2][2] = {};
     // occupancy of the selection kernel per (warp-queue width class, bf16)
     int occ_select[4][2] = {};
+    size_t occ_select_smem[4][2] = {};  // the shared memory each was measured at
 };
 
 namespace {
@@ -184,19 +186,37 @@ ssb_status run(ssb_context * ctx, const ssb_rows * r, const Debug * dbg, cudaStr
     sa.cap = mode == 1 ? (int) div_up(kb + std::max(1024, kb), 32) * 32 : 0;
     sa.sel_slots = mode == 1 ? ssb::next_pow2(std::max(kb, 2)) : 0;
     // aligned rows with a small top-k (or all greedy) take the warp-specialized selection kernel
-    const bool use_select = vec && (mode == 0 || kb <= ssb::kSelectMaxK);
+    bool use_select = vec && (mode == 0 || kb <= ssb::kSelectMaxK);
     const int kw = use_select ? ssb::select_kw(kb, mode == 0) : -1;
-    int & occ = use_select ? ctx->occ_select[kw == 0 ? 0 : (kw == 1 ? 1 : (kw == 2 ? 2 : 3))][bf16] : ctx->occupancy[mode][bf16][vec];
-    if (occ == 0) {
-        const int full_chunk = (int) div_up(r->vocab, 32) * 32;
-        occ = use_select ? ssb::select_blocks_per_sm(kw, bf16, ssb::select_smem_bytes(kw, bf16, full_chunk, sa.hist_slots, sa.sel_slots))
-                         : ssb::stream_blocks_per_sm(mode, bf16, vec,
-                                                     ssb::stream_smem_bytes(mode, vec, full_chunk, sa.hist_slots, sa.cap, sa.sel_slots));
+    const int full_chunk = (int) div_up(r->vocab, 32) * 32;
+    // the selection kernels keep per-chunk state in shared memory: cap the chunk so that it fits
+    int max_chunk = full_chunk;
+    if (use_select) {
+        max_chunk = std::min(full_chunk, ssb::select_max_chunk(kw, bf16));
+        while (max_chunk > 4096 && ssb::select_smem_bytes(kw, bf16, max_chunk, sa.hist_slots, sa.sel_slots) > (size_t) ctx->max_smem)
+            max_chunk = (int) div_up(max_chunk / 2, 32) * 32;
+        if (ssb::select_smem_bytes(kw, bf16, max_chunk, sa.hist_slots, sa.sel_slots) > (size_t) ctx->max_smem) use_select = false;
+    }
+    int occ_select_now = 0;
+    int & occ = use_select ? occ_select_now : ctx->occupancy[mode][bf16][vec];
+    if (use_select) {
+        // per history size, so measured for this call's shared memory (a cached value per width class)
+        int & cached = ctx->occ_select[kw == 0 ? 0 : (kw == 1 ? 1 : (kw == 2 ? 2 : 3))][bf16];
+        const size_t smem = ssb::select_smem_bytes(kw, bf16, max_chunk, sa.hist_slots, sa.sel_slots);
+        if (cached == 0 || ctx->occ_select_smem[kw == 0 ? 0 : (kw == 1 ? 1 : (kw == 2 ? 2 : 3))][bf16] != smem) {
+            cached = ssb::select_blocks_per_sm(kw, bf16, smem);
+            ctx->occ_select_smem[kw == 0 ? 0 : (kw == 1 ? 1 : (kw == 2 ? 2 : 3))][bf16] = smem;
+        }
+        occ = cached;
+        if (occ <= 0) return fail(SSB_DEVICE, "the selection kernel does not fit on this device");
+    } else if (occ == 0) {
+        occ = ssb::stream_blocks_per_sm(mode, bf16, vec, ssb::stream_smem_bytes(mode, vec, full_chunk, sa.hist_slots, sa.cap, sa.sel_slots));
         if (occ <= 0) return fail(SSB_DEVICE, "the streaming kernel does not fit on this device");
     }
     const int slots = std::min(ctx->max_slots, ctx->sm_count * occ);
     const int min_chunk = mode == 0 ? 2048 : 4096;
     int64_t splits = std::max<int64_t>(1, std::min<int64_t>(div_up(r->vocab, min_chunk), slots / std::max(1, r->rows)));
+    splits = std::max<int64_t>(splits, div_up(r->vocab, max_chunk));
     int64_t chunk = div_up(div_up(r->vocab, splits), 32) * 32;
     splits = div_up(r->vocab, chunk);
     sa.splits = (int) splits;
@@ -260,6 +280,7 @@ ssb_status ssb_context_create(int32_t device, ssb_context ** out) {
         return s;
     }
     e = cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&ctx->max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
     if (e != cudaSuccess) {
         delete ctx;
         return cuda_fail(e, "cudaDeviceGetAttribute");

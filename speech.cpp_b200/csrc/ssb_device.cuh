@@ -211,6 +211,32 @@ __device__ __forceinline__ int block_or(int v, int * scratch) {
     return __any_sync(0xffffffffu, lane_id() < nw ? scratch[lane_id()] : 0);
 }
 
+__device__ __forceinline__ int block_sum_int(int v, int * scratch) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();
+    if (lane_id() == 0) scratch[warp_id()] = v;
+    __syncthreads();
+    const int nw = blockDim.x >> 5;
+    int t = lane_id() < nw ? scratch[lane_id()] : 0;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    return t;
+}
+
+__device__ __forceinline__ int block_max_int(int v, int * scratch) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+    __syncthreads();
+    if (lane_id() == 0) scratch[warp_id()] = v;
+    __syncthreads();
+    const int nw = blockDim.x >> 5;
+    int t = lane_id() < nw ? scratch[lane_id()] : INT_MIN;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) t = max(t, __shfl_xor_sync(0xffffffffu, t, o));
+    return t;
+}
+
 // ---------------------------------------------------------------- radix select on composites
 // Shared state of one selection.
 struct SelectState {

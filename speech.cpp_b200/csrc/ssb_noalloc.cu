@@ -53,6 +53,7 @@ struct DeviceSetup {
     bool ready = false;
     unsigned char * scratch = nullptr;  // g_scratch's device address on this device
     int sm_count = 0;
+    int max_smem = 0;  // opt-in shared memory per block
 };
 
 DeviceSetup g_setup[kMaxDevices];
@@ -77,6 +78,7 @@ ssb_status setup(int device, DeviceSetup ** out) {
         cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);
         if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_scratch)");
         e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, device);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&d.max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
         if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
         d.scratch = static_cast<unsigned char *>(p);
         d.ready = true;
@@ -162,11 +164,16 @@ extern "C" ssb_status ssb_sample_rows_noalloc(const ssb_rows * r, void * stream_
     sa.hist_slots = r->history ? ssb::next_pow2((int) std::max<int64_t>(4, 2 * r->history_ld)) : 0;
     sa.sel_slots = ssb::next_pow2(std::max(kb, 2));
     const int full_chunk = (int) div_up(r->vocab, 32) * 32;
-    const int occ = ssb::select_blocks_per_sm(kw, bf16, ssb::select_smem_bytes(kw, bf16, full_chunk, sa.hist_slots, sa.sel_slots));
+    const int max_chunk = std::min(full_chunk, ssb::select_max_chunk(kw, bf16));
+    const size_t smem = ssb::select_smem_bytes(kw, bf16, max_chunk, sa.hist_slots, sa.sel_slots);
+    if (smem > (size_t) d->max_smem)
+        return fail(SSB_OUT_OF_RANGE, "the history is too long for the selection kernel's shared memory; use ssb_sample_rows");
+    const int occ = ssb::select_blocks_per_sm(kw, bf16, smem);
     if (occ <= 0) return fail(SSB_DEVICE, "the selection kernel does not fit on this device");
     const int slots = std::min(kScratchSlots, d->sm_count * occ);
     const int min_chunk = all_greedy ? 2048 : 4096;
     int64_t splits = std::max<int64_t>(1, std::min<int64_t>(div_up(r->vocab, min_chunk), slots / std::max(1, r->rows)));
+    splits = std::max<int64_t>(splits, div_up(r->vocab, max_chunk));
     const int64_t chunk = div_up(div_up(r->vocab, splits), 32) * 32;
     splits = div_up(r->vocab, chunk);
     sa.splits = (int) splits;

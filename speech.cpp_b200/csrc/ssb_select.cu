@@ -467,6 +467,8 @@ int select_kw(int k_bound, bool all_greedy) {
     return k_bound <= 32 ? 1 : (k_bound <= 64 ? 2 : 4);
 }
 
+int select_max_chunk(int kw, bool bf16) { return kw > 0 ? topk_max_chunk(bf16) : 262144; }
+
 size_t select_smem_bytes(int kw, bool bf16, int chunk, int hist_slots, int sel_slots) {
     if (kw > 0) return topk_smem_bytes(kw, bf16, chunk, hist_slots, sel_slots);
     const size_t hwords = (size_t) ((((chunk + 31) >> 5) + 3) & ~3);

@@ -4,36 +4,39 @@
 // One CTA streams `chunk` consecutive columns of one row (several CTAs per row when the batch is small;
 // the last to finish merges their lists, as in ssb_stream.cu). Two passes:
 //
-// Pass 1, the stream (warp-specialized). A producer warp brings the chunk through a ring of kStages
-// 16 KB shared-memory stages with TMA bulk copies (cp.async.bulk + mbarrier complete_tx) and refills a
-// slot as soon as every consumer warp has copied its part into registers. Each of 256 consumer lanes
-// takes four 16-byte groups per stage (a "block" of 32 bf16 or 16 fp32 logits) and only
-//   * stores the block's NaN-propagating maximum, rounded up to bf16 (an upper bound of every logit
-//     in it), and
-//   * keeps its own two largest block maxima among blocks without a masked or history token ("plain"
-//     blocks: their raw logits are their restricted logits, qwen3-tts/sampler.cpp:29-51).
-// No thresholds, no data-dependent branches: the stream runs at the rate the ring is filled.
+// Before the stream: the row's history table (distinct ids with their counts) and a bitmap of the
+// blocks holding a history or a masked token ("special" blocks; every other block's raw logits are its
+// restricted logits, qwen3-tts/sampler.cpp:29-51), built by all threads while the first stages load.
 //
-// End phase (block-wide, short loops).
-//   E1  bound: radix select (two 8-bit digits) of the k-th largest of the lanes' kept maxima. They are
-//       restricted logits of distinct tokens, so k tokens reach the selected prefix s_b, and for a
-//       positive temperature (which keeps the order) k scaled logits reach c = fl(s_b / T) — so the k
-//       best all have a scaled logit >= c.
-//   E2  history tokens (their penalized and masked logits were computed by the producer warp during the
-//       stream, from the logits the stream had just brought into L2): candidates if they reach c.
-//   E3  pass 2: the blocks whose maximum can reach c are read again (from L2) and every element that is
-//       not a history token is restricted (-inf where masked), divided by the temperature exactly as
+// Pass 1, the stream. A producer warp brings the chunk through a ring of kTkStages 16 KB shared-memory
+// stages with TMA bulk copies (cp.async.bulk + mbarrier complete_tx) and refills a slot as soon as every
+// consumer warp has copied its part into registers. Each of 256 consumer lanes takes four 16-byte groups
+// per stage (a "block" of 32 bf16 or 16 fp32 logits), stores the block's NaN-propagating maximum
+// rounded up to bf16 (an upper bound of every logit in it) and keeps its two largest plain block maxima.
+//
+// End phase (short, mostly warp-local).
+//   E1  bound: the lanes' kept maxima are 512 restricted logits of distinct tokens (for fp32 rows the
+//       largest bf16 at or below each); the k-th largest of them by a 16-step bisection on their
+//       order keys is s_b. k tokens reach s_b, so for a positive temperature
+//       (which keeps the order) every one of the k best has a scaled logit >= c = fl(s_b / T).
+//   E2  history tokens: penalized (and masked) logits computed now, from the logits the stream has just
+//       brought into L2; candidates if they reach c.
+//   E3  pass 2: the blocks whose maximum can reach c form a list; each lane reads one 16-byte group of
+//       them again (from L2), eight blocks per warp and round. Every element that
+//       is not a history token is restricted (-inf where masked), divided by the temperature exactly as
 //       the reference does (qwen3-tts/sampler.cpp:73) and keyed as a composite (value, then lowest
 //       index: the order of qwen3-tts/sampler.cpp:78-79 with haru/sampler.cpp:39's tie-break).
-//       Composites >= the threshold go to a candidate array (the ring's memory); an array that could
-//       overflow is cut to its k best by a radix select, which also raises the threshold.
+//       Composites >= the threshold go to a candidate array in the ring's memory. When the qualifying
+//       blocks could overflow it (or the list), the rounds are synchronized and the array is cut to
+//       its k best by a radix select (which also raises the threshold) between them.
 //   E4  columns past the last whole 16-byte group.
-//   E5  the candidates are sorted (bitonic, or radix-selected to k first), and finalize_draw replays
-//       the reference's double-precision softmax, top-p cut and pick.
+//   E5  the candidates are ranked (each against all: they are few and distinct), and finalize_draw
+//       replays the reference's double-precision softmax, top-p cut and pick.
 // The restricted maximum (for the row statuses, qwen3-tts/sampler.cpp:43-49) is exact: the largest
 // restricted logit lies in a block whose maximum reaches c, or is a history token.
 // Temperatures that do not keep the order (<= 0 or NaN) make every block a pass-2 block.
 #include <climits>
+#include <type_traits>
 #include <cuda_bf16.h>
 
 #include "ssb_device.cuh"
@@ -45,10 +48,12 @@ namespace ssb {
 namespace {
 
 constexpr int kTkStages = 4;
+constexpr int kTkThreads = kStreamCtaThreads;      // 8 consumer warps + the producer warp
 constexpr int kCap = kTkStages * kStageBytes / 8;  // candidate composites the ring's memory holds
-constexpr int kHistChunk = 8;                      // history slots per thread between overflow checks
-constexpr int kRoom = 2304;                        // most candidates one E2 chunk or E3 round adds
-static_assert(kRoom >= kStreamCtaThreads * kHistChunk && kRoom >= kConsumerWarps * 32 * 8, "room for one round");
+constexpr int kMaxStages = 64;                     // stages of one chunk (a lane's pass-2 mask is 64-bit)
+constexpr int kRankMax = kTkThreads;               // candidates ranked directly (one per thread)
+constexpr int kListMax = 1024;                     // pass-2 blocks listed for the cooperative rounds
+constexpr int kRoundBlocks = kConsumerWarps * 8;   // blocks per cooperative round
 
 // bf16 bits of the smallest bf16 >= x (NaN stays NaN): block maxima kept in 16 bits as upper bounds.
 __device__ __forceinline__ uint16_t bf16_up(float x) {
@@ -81,10 +86,11 @@ __device__ __forceinline__ int hist_slot(const int32_t * keys, int bits, int32_t
 }
 
 template <typename TIn, int KW, bool kDebug>
-__global__ void __launch_bounds__(kStreamCtaThreads, 2) topk_rows_kernel(const StreamArgs sa) {
+__global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamArgs sa) {
     const RowsArgs & a = sa.r;
     constexpr int G = Elem<TIn>::kVec;
     constexpr int kStageElems = kStageBytes / (int) sizeof(TIn);
+    constexpr int kBlockElems = kGroupsPerThread * G;
     constexpr int QN = KW;  // registers per lane of a sorted list of 32*QN
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t s_full[kTkStages];
@@ -92,11 +98,13 @@ __global__ void __launch_bounds__(kStreamCtaThreads, 2) topk_rows_kernel(const S
     __shared__ SelectState sel;
     __shared__ float s_redf[32];
     __shared__ int s_redi[32];
-    __shared__ int s_count, s_gather, s_abort, s_last, s_n0;
+    __shared__ int s_count, s_gather, s_abort, s_last, s_n0, s_qn;
+    __shared__ int s_qlist[kListMax];
+    __shared__ uint32_t s_keys[2 * kConsumers];  // E1 (not ring memory: a slower warp may still read its last stage)
 
     const int tid = (int) threadIdx.x;
     const int warp = warp_id(), lane = lane_id();
-    const bool producer = warp == kConsumerWarps;
+    const bool consumer = warp < kConsumerWarps;
     const int splits = sa.splits;
     const int row = blockIdx.x / splits;
     const int split = blockIdx.x - row * splits;
@@ -118,23 +126,34 @@ __global__ void __launch_bounds__(kStreamCtaThreads, 2) topk_rows_kernel(const S
     const int nvec = len / G;  // whole 16-byte groups; the rest are tail columns
     const int nstages = (nvec + kStageGroups - 1) / kStageGroups;
 
-    // ---- shared memory: [ring = candidates later] [block maxima, bf16] [special-block bitmap]
-    //                     [hash keys] [hash counts -> penalized logits] [selected]
+    // ---- shared memory: [ring = candidates once the stream is over] [block maxima, bf16] [special-block bitmap]
+    //                     [hash keys] [hash counts] [selected]
     const int nst_alloc = (sa.chunk * (int) sizeof(TIn) + kStageBytes - 1) / kStageBytes;
     unsigned char * ring = smem;
     uint64_t * s_cand = reinterpret_cast<uint64_t *>(smem);  // [kCap], once the stream is over
-    float * s_keep = reinterpret_cast<float *>(smem);        // [2 * kConsumers], E1 only
     uint16_t * s_up = reinterpret_cast<uint16_t *>(smem + kTkStages * kStageBytes);  // [nst_alloc][kConsumers]
     uint32_t * s_bb = reinterpret_cast<uint32_t *>(s_up + nst_alloc * kConsumers);  // [nst_alloc][kConsumerWarps]
     int32_t * s_hkey = reinterpret_cast<int32_t *>(s_bb + nst_alloc * kConsumerWarps);
-    int32_t * s_hval = s_hkey + sa.hist_slots;
-    uint64_t * s_sel = reinterpret_cast<uint64_t *>(s_hval + sa.hist_slots);  // [max(sel_slots, 32*QN)]
+    int32_t * s_hcnt = s_hkey + sa.hist_slots;
+    uint64_t * s_sel = reinterpret_cast<uint64_t *>(s_hcnt + sa.hist_slots);  // [max(sel_slots, 32*QN)]
 
     const TIn * src = reinterpret_cast<const TIn *>(a.logits) + (int64_t) row * a.ld;
     const char * gsrc = reinterpret_cast<const char *>(src + c0);
 
+    const int32_t * hist = a.history ? a.history + (int64_t) row * a.history_ld : nullptr;
+    int hlen = 0;
+    if (hist) {
+        hlen = a.history_len ? a.history_len[row] : (int) a.history_ld;
+        hlen = hlen < 0 ? 0 : (hlen > (int) a.history_ld ? (int) a.history_ld : hlen);
+    }
+    const bool penal = p.history_applies && hlen > 0;
+    const uint32_t * mrow = (a.mask && a.mask_kind != SSB_MASK_NONE) ? a.mask + (int64_t) row * a.mask_ld : nullptr;
+    const bool special = mrow != nullptr || penal;
+    const int hbits_n = sa.hist_slots > 1 ? 31 - __clz(sa.hist_slots) : 1;
+
     if (tid == 0) {
         s_count = 0;
+        s_qn = 0;
         s_abort = 0;
         for (int q = 0; q < kTkStages; q++) mbar_init(&s_full[q], 1), mbar_init(&s_empty[q], kConsumerWarps);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -146,30 +165,19 @@ __global__ void __launch_bounds__(kStreamCtaThreads, 2) topk_rows_kernel(const S
         }
     }
 
-    // ---- special blocks: history tokens (hash table of distinct ids with their counts) and masked
-    //      tokens, marked per block for pass 1
-    const int32_t * hist = a.history ? a.history + (int64_t) row * a.history_ld : nullptr;
-    int hlen = 0;
-    if (hist) {
-        hlen = a.history_len ? a.history_len[row] : (int) a.history_ld;
-        hlen = hlen < 0 ? 0 : (hlen > (int) a.history_ld ? (int) a.history_ld : hlen);
-    }
-    const bool penal = p.history_applies && hlen > 0;
-    const uint32_t * mrow = (a.mask && a.mask_kind != SSB_MASK_NONE) ? a.mask + (int64_t) row * a.mask_ld : nullptr;
-    const bool special = mrow != nullptr || penal;
-    const int hbits_n = sa.hist_slots > 1 ? 31 - __clz(sa.hist_slots) : 1;
+    // ---- special blocks (all threads, while the first stages load)
     if (special) {
         for (int i = tid; i < nstages * kConsumerWarps; i += blockDim.x) s_bb[i] = 0;
         if (penal)
-            for (int i = tid; i < sa.hist_slots; i += blockDim.x) s_hkey[i] = -1, s_hval[i] = 0;
+            for (int i = tid; i < sa.hist_slots; i += blockDim.x) s_hkey[i] = -1, s_hcnt[i] = 0;
         __syncthreads();
         if (penal) {
             const uint32_t hmask = (uint32_t) sa.hist_slots - 1u;
-            for (int base = 0; base < hlen; base += 4 * kStreamCtaThreads) {  // warp-uniform trip count
+            for (int base = 0; base < hlen; base += 4 * kTkThreads) {  // warp-uniform trip count
                 int32_t t[4];
 #pragma unroll
                 for (int q = 0; q < 4; q++) {  // four independent loads in flight
-                    const int i = base + q * kStreamCtaThreads + tid;
+                    const int i = base + q * kTkThreads + tid;
                     t[q] = i < hlen ? __ldg(hist + i) : -1;
                 }
 #pragma unroll
@@ -183,7 +191,7 @@ __global__ void __launch_bounds__(kStreamCtaThreads, 2) topk_rows_kernel(const S
                             for (uint32_t n = 0; n <= hmask; n++) {
                                 const int32_t old = atomicCAS(&s_hkey[h], -1, t[q]);
                                 if (old == -1 || old == t[q]) {
-                                    atomicAdd(&s_hval[h], __popc(peers));
+                                    atomicAdd(&s_hcnt[h], __popc(peers));
                                     break;
                                 }
                                 h = (h + 1) & hmask;
@@ -192,6 +200,7 @@ __global__ void __launch_bounds__(kStreamCtaThreads, 2) topk_rows_kernel(const S
                             if (gi < nvec) atomicOr(&s_bb[block_word(gi)], 1u << (gi & 31));
                         }
                     }
+                    __syncwarp();
                 }
             }
         }
@@ -200,16 +209,16 @@ __global__ void __launch_bounds__(kStreamCtaThreads, 2) topk_rows_kernel(const S
             constexpr int kGroupsPerWord = 32 / G;
             constexpr uint32_t gfull = (1u << G) - 1u;
             const int w0 = c0 >> 5, nw = (len + 31) >> 5;
-            for (int base = 0; base < nw; base += 4 * kStreamCtaThreads) {
+            for (int base = 0; base < nw; base += 4 * kTkThreads) {
                 uint32_t mw[4];
 #pragma unroll
                 for (int q = 0; q < 4; q++) {
-                    const int i = base + q * kStreamCtaThreads + tid;
+                    const int i = base + q * kTkThreads + tid;
                     mw[q] = i < nw ? __ldg(mrow + w0 + i) : 0u;
                 }
 #pragma unroll
                 for (int q = 0; q < 4; q++) {
-                    const int i = base + q * kStreamCtaThreads + tid;
+                    const int i = base + q * kTkThreads + tid;
                     const int gi0 = i * kGroupsPerWord;
                     if (i < nw && gi0 < nvec) {
                         uint32_t sb = 0;
@@ -224,6 +233,7 @@ __global__ void __launch_bounds__(kStreamCtaThreads, 2) topk_rows_kernel(const S
                 }
             }
         }
+        __syncwarp();
     }
     __syncthreads();
 
@@ -235,8 +245,9 @@ __global__ void __launch_bounds__(kStreamCtaThreads, 2) topk_rows_kernel(const S
     };
 
     // ---- pass 1
-    float keep0 = -kInf, keep1 = -kInf;  // the lane's two largest plain block maxima
-    if (producer) {
+    uint32_t key0 = 0, key1 = 0;  // the lane's two largest plain block maxima (16-bit order keys; 0: none)
+    if (!consumer) {
+        // producer
         if (lane == 0) {
             for (int st = kTkStages; st < nstages; st++) {
                 const int slot = st % kTkStages;
@@ -245,30 +256,6 @@ __global__ void __launch_bounds__(kStreamCtaThreads, 2) topk_rows_kernel(const S
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 mbar_expect(&s_full[slot], bytes);
                 bulk_load(ring + slot * kStageBytes, gsrc + (size_t) st * kStageBytes, bytes, &s_full[slot]);
-            }
-        }
-        __syncwarp();
-        // every stage is issued: the penalized (and masked) logits of the history tokens, from the
-        // logits the stream has brought into L2
-        if (penal) {
-            for (int base = 0; base < sa.hist_slots; base += 32 * 8) {
-                int32_t t[8];
-                float raw[8];
-#pragma unroll
-                for (int q = 0; q < 8; q++) {
-                    const int i = base + q * 32 + lane;
-                    t[q] = i < sa.hist_slots ? s_hkey[i] : -1;
-                }
-#pragma unroll
-                for (int q = 0; q < 8; q++) raw[q] = t[q] >= 0 ? Elem<TIn>::load1(src, t[q]) : 0.0f;
-#pragma unroll
-                for (int q = 0; q < 8; q++) {
-                    if (t[q] >= 0) {
-                        const int i = base + q * 32 + lane;
-                        const float v = masked(t[q]) ? -kInf : penalize(raw[q], s_hval[i], p);
-                        s_hval[i] = __float_as_int(v);
-                    }
-                }
             }
         }
     } else {
@@ -284,36 +271,54 @@ __global__ void __launch_bounds__(kStreamCtaThreads, 2) topk_rows_kernel(const S
                 const int g = j * kConsumers + tid;
                 rv[j] = g < sgroups ? stage[g] : neg_inf_group<TIn>();
             }
-            const bool spb = special && ((s_bb[st * kConsumerWarps + warp] >> lane) & 1u);
             // the lane's part of the stage is in registers: release the slot to the producer
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_empty[slot]);
             if (++slot == kTkStages) slot = 0, phase ^= 1u;
             const float lm = lane_max<TIn>(rv);
-            s_up[st * kConsumers + tid] = bf16_up(lm);
-            const float v = (spb || lm != lm) ? -kInf : lm;
-            if (v > keep1) {
-                keep1 = v > keep0 ? keep0 : v;
-                keep0 = v > keep0 ? v : keep0;
+            const uint16_t up = bf16_up(lm);
+            s_up[st * kConsumers + tid] = up;
+            const bool plain = !(special && ((s_bb[st * kConsumerWarps + warp] >> lane) & 1u)) && lm == lm;
+            // a plain block's maximum, as the key of a bf16 at or below it (fp32 maxima were rounded up)
+            const uint32_t kb = (order_key(__uint_as_float((uint32_t) up << 16)) >> 16) -
+                                ((sizeof(TIn) == 4 && lm > -kInf) ? 1u : 0u);
+            if (plain && kb > key1) {
+                key1 = kb > key0 ? key0 : kb;
+                key0 = kb > key0 ? kb : key0;
             }
         }
     }
+    __syncwarp();
 
     // ---- end phase (all threads)
+    if (consumer) s_keys[tid] = key0, s_keys[kConsumers + tid] = key1;
     __syncthreads();
-    if (!producer) s_keep[tid] = keep0, s_keep[kConsumers + tid] = keep1;
-    __syncthreads();
-    // E1: a bound that k restricted logits reach
-    radix_select(2 * kConsumers, k, [&](int i) { return (uint64_t) order_key(s_keep[i]) << 32; }, sel, 2);
-    const uint32_t sb_key = (uint32_t) (sel.prefix >> 32);
-    const float s_b = sb_key <= order_key(-kInf) ? -kInf : key_value(sb_key);
-    __syncthreads();  // s_keep is ring memory, about to hold candidates
+    // E1: the largest 16-bit key P that at least k of the 512 reach (every warp computes it)
+    uint32_t P = 0;
+    {
+        uint32_t kv[2 * kConsumers / 32];
+#pragma unroll
+        for (int q = 0; q < 2 * kConsumers / 32; q++) kv[q] = s_keys[q * 32 + lane];
+#pragma unroll 1
+        for (int b = 15; b >= 0; b--) {
+            const uint32_t cand = P | (1u << b);
+            uint32_t n = 0;
+#pragma unroll
+            for (int q = 0; q < 2 * kConsumers / 32; q++) n += kv[q] >= cand;
+            if (__reduce_add_sync(0xffffffffu, n) >= (uint32_t) k) P = cand;
+        }
+    }
+    // P <= key of -inf (no k keys): no bound; else the value of key P << 16 is at or below k restricted
+    // logits
+    const float s_b = (P << 16) <= order_key(-kInf) ? -kInf : key_value(P << 16);
     const float T = greedy_row ? 1.0f : p.temperature;
     const bool scale = !greedy_row;
     const bool fast = greedy_row ? true : p.fast_scale;
     const bool monotone = greedy_row || T > 0.0f;
-    uint64_t theta = composite(monotone && scale ? __fdiv_rn(s_b, T) : (monotone ? s_b : -kInf), 0xFFFFFFFFu);
-    float cs = composite_value(theta);  // scaled logits below cs cannot be among the k best
+    float c_init = monotone ? (scale ? __fdiv_rn(s_b, T) : s_b) : -kInf;
+    if (c_init != c_init) c_init = -kInf;
+    uint64_t theta = composite(c_init, 0xFFFFFFFFu);
+    float cs = composite_value(theta);               // scaled logits below cs cannot be among the k best
     float rb = scale ? raw_bound(cs, T, fast) : cs;  // raw logits below rb cannot reach cs
     auto raise = [&](uint64_t t) {
         if (t > theta) {
@@ -331,30 +336,51 @@ __global__ void __launch_bounds__(kStreamCtaThreads, 2) topk_rows_kernel(const S
 
     float acc = -kInf;  // restricted maximum
     int nan_scaled = 0;
-    // one candidate per lane where `has`, appended by one shared atomic per warp
-    auto append = [&](bool has, uint64_t cv) {
-        const unsigned m = __ballot_sync(0xffffffffu, has);
-        if (!m) return;
-        const int leader = __ffs(m) - 1;
+    // each lane's candidates (cv[i] where bit i of vm is set), appended by one shared atomic per warp
+    auto append_m = [&](uint32_t vm, const uint64_t * cv, auto n_tag) {
+        constexpr int N = decltype(n_tag)::value;
+        const int n = __popc(vm);
+        int incl = n;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t;
+        }
+        const int total = __shfl_sync(0xffffffffu, incl, 31);
         int base = 0;
-        if (lane == leader) base = atomicAdd(&s_count, __popc(m));
-        base = __shfl_sync(0xffffffffu, base, leader);
-        if (has) s_cand[base + __popc(m & ((1u << lane) - 1u))] = cv;
+        if (lane == 31) base = atomicAdd(&s_count, total);
+        base = __shfl_sync(0xffffffffu, base, 31) + incl - n;
+#pragma unroll
+        for (int i = 0; i < N; i++)
+            if ((vm >> i) & 1u) s_cand[base + __popc(vm & ((1u << i) - 1u))] = cv[i];
     };
-    // restricted logit v of column col: statistics, and a candidate if its composite reaches theta
-    auto consider = [&](bool valid, float v, int col) {
-        bool has = false;
-        uint64_t cv = 0;
-        if (valid) {
-            acc = max_nan(acc, v);
-            if (v >= rb) {
-                const float sc = scale ? __fdiv_rn(v, T) : v;
-                nan_scaled |= sc != sc;
-                cv = composite(sc, (uint32_t) col);
-                has = cv >= theta;
+    // restricted logit v of column col: statistics, and whether its composite reaches theta
+    auto test = [&](float v, int col, uint64_t & cv) {
+        acc = max_nan(acc, v);
+        if (!(v >= rb)) return false;
+        const float sc = scale ? __fdiv_rn(v, T) : v;
+        nan_scaled |= sc != sc;
+        cv = composite(sc, (uint32_t) col);
+        return cv >= theta;
+    };
+    // one 16-byte group of restricted-candidate elements (history elements are skipped: taken in E2)
+    auto take_group = [&](bool live, const uint4 & raw, int col0, bool blk_special) {
+        uint64_t cv[G];
+        uint32_t vm = 0;
+        if (live) {
+            float v[G];
+            Elem<TIn>::unpack(raw, v);
+#pragma unroll
+            for (int e = 0; e < G; e++) {
+                bool skip = false;
+                if (blk_special) {
+                    if (penal && hist_slot(s_hkey, hbits_n, col0 + e) >= 0) skip = true;
+                    else if (masked(col0 + e)) v[e] = -kInf;
+                }
+                if (!skip && test(v[e], col0 + e, cv[e])) vm |= 1u << e;
             }
         }
-        append(has, cv);
+        if (__any_sync(0xffffffffu, vm != 0)) append_m(vm, cv, std::integral_constant<int, G>());
     };
     // cuts the candidates to their k best (block-wide) and raises the threshold to the k-th
     auto cut = [&]() {
@@ -377,105 +403,144 @@ __global__ void __launch_bounds__(kStreamCtaThreads, 2) topk_rows_kernel(const S
 
     // E2: history tokens
     if (penal) {
-        for (int base = 0; base < sa.hist_slots; base += kHistChunk * (int) blockDim.x) {
-#pragma unroll 1
-            for (int q = 0; q < kHistChunk; q++) {
-                const int i = base + q * (int) blockDim.x + tid;
-                const int32_t t = i < sa.hist_slots ? s_hkey[i] : -1;
-                consider(t >= 0, t >= 0 ? __int_as_float(s_hval[i]) : 0.0f, t);
+        for (int base = 0; base < sa.hist_slots; base += 8 * kTkThreads) {  // uniform
+            int32_t t[8];
+            float raw[8];
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+                const int i = base + q * kTkThreads + tid;
+                t[q] = i < sa.hist_slots ? s_hkey[i] : -1;
             }
+#pragma unroll
+            for (int q = 0; q < 8; q++) raw[q] = t[q] >= 0 ? Elem<TIn>::load1(src, t[q]) : 0.0f;
+            uint64_t cv[8];
+            uint32_t vm = 0;
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+                if (t[q] >= 0) {
+                    const int i = base + q * kTkThreads + tid;
+                    const float v = masked(t[q]) ? -kInf : penalize(raw[q], s_hcnt[i], p);
+                    if (test(v, t[q], cv[q])) vm |= 1u << q;
+                }
+            }
+            if (__any_sync(0xffffffffu, vm != 0)) append_m(vm, cv, std::integral_constant<int, 8>());
+            __syncwarp();
             __syncthreads();
-            if (s_count > kCap - kRoom) cut();
+            if (s_count > kCap - 8 * kTkThreads) cut();
         }
     }
 
-    // E3: pass 2 over the blocks whose maximum can reach the threshold; each consumer warp walks its
-    // own blocks, eight per round (lane l takes group l & 3 of block l >> 2)
-    int gst = 0, gqst = 0;
-    unsigned gq = 0;
-    bool more = !producer && nstages > 0;
-    while (__syncthreads_or(more)) {
-        if (more) {
-            int n = 0, my_blk = 0;
-            while (n < 8) {  // warp-uniform
-                if (gq == 0) {
-                    if (gst >= nstages) break;
-                    const float up = __uint_as_float((uint32_t) s_up[gst * kConsumers + warp * 32 + lane] << 16);
-                    gq = __ballot_sync(0xffffffffu, qualifies(up));
-                    gqst = gst++;
-                    continue;
-                }
-                const int b = __ffs(gq) - 1;
-                gq &= gq - 1u;
-                if (lane == n) my_blk = (gqst << 5) | b;
-                n++;
-            }
-            more = gq != 0 || gst < nstages;
-            const int blk = __shfl_sync(0xffffffffu, my_blk, lane >> 2);
-            const int bst = blk >> 5, bl = blk & 31;
-            const int g = (lane & 3) * kConsumers + warp * 32 + bl;
-            const bool has = (lane >> 2) < n && g < min(kStageGroups, nvec - bst * kStageGroups);
-            const int col0 = c0 + bst * kStageElems + g * G;
-            float v[G];
-            uint32_t hist_e = 0;  // history elements: taken in E2
-            if (has) {
-                Elem<TIn>::unpack(__ldcg(reinterpret_cast<const uint4 *>(src + col0)), v);
-                if (special && ((s_bb[bst * kConsumerWarps + warp] >> bl) & 1u)) {
-#pragma unroll
-                    for (int e = 0; e < G; e++) {
-                        if (penal && hist_slot(s_hkey, hbits_n, col0 + e) >= 0) hist_e |= 1u << e;
-                        else if (masked(col0 + e)) v[e] = -kInf;
-                    }
-                }
-            }
-#pragma unroll
-            for (int e = 0; e < G; e++) consider(has && !((hist_e >> e) & 1u), has ? v[e] : 0.0f, col0 + e);
+    // E3: pass 2 over the blocks whose maximum can reach the threshold
+    uint64_t qmask = 0;  // stages of this lane's qualifying blocks
+    if (consumer)
+        for (int st = 0; st < nstages; st++)
+            if (qualifies(__uint_as_float((uint32_t) s_up[st * kConsumers + tid] << 16))) qmask |= 1ull << st;
+    const int nq = __popcll(qmask);
+    if (nq > 0) {
+        const int at = atomicAdd(&s_qn, nq);
+        uint64_t m = qmask;
+        for (int i = 0; i < nq && at + i < kListMax; i++) {
+            const int st = __ffsll((long long) m) - 1;
+            m &= m - 1;
+            s_qlist[at + i] = (st << 9) | tid;
         }
-        __syncthreads();
-        if (s_count > kCap - kRoom) cut();
+    }
+    __syncwarp();
+    __syncthreads();
+    const int qtotal = s_qn;
+    const bool synced = s_count + qtotal * kBlockElems + G > kCap;
+    if (synced && s_count > kCap - kConsumers * G) cut();
+    if (qtotal <= kListMax) {
+        // cooperative rounds: a consumer warp takes eight listed blocks, lane l group l & 3 of block l >> 2
+        const int rounds = (qtotal + kRoundBlocks - 1) / kRoundBlocks;
+        for (int r = 0; r < rounds; r++) {  // CTA-uniform
+            if (consumer) {
+                const int e = r * kRoundBlocks + warp * 8 + (lane >> 2);
+                const int j = lane & 3;
+                bool live = false;
+                uint4 raw = make_uint4(0, 0, 0, 0);
+                int col0 = c0;
+                bool blk_special = false;
+                if (e < qtotal) {
+                    const int ent = s_qlist[e];
+                    const int st = ent >> 9, t = ent & 511;
+                    const int g = j * kConsumers + t;
+                    col0 = c0 + st * kStageElems + g * G;
+                    live = g < min(kStageGroups, nvec - st * kStageGroups);
+                    if (live) raw = __ldcg(reinterpret_cast<const uint4 *>(src + col0));
+                    blk_special = special && ((s_bb[st * kConsumerWarps + (t >> 5)] >> (t & 31)) & 1u);
+                }
+                take_group(live, raw, col0, blk_special);
+            }
+            if (synced) {
+                __syncwarp();
+                __syncthreads();
+                if (s_count > kCap - kConsumers * G) cut();
+            }
+        }
+    } else {
+        // a list that long (no useful bound): each lane takes its own blocks, one group per round
+        const int passes = block_max_int(nq, s_redi);
+        for (int pass = 0; pass < passes; pass++) {  // CTA-uniform
+            const bool has = qmask != 0;
+            const int st = has ? __ffsll((long long) qmask) - 1 : 0;
+            qmask &= qmask - 1;
+            const bool blk_special = has && special && ((s_bb[st * kConsumerWarps + warp] >> lane) & 1u);
+            for (int j = 0; j < kGroupsPerThread; j++) {
+                const int g = j * kConsumers + tid;
+                const int col0 = c0 + st * kStageElems + g * G;
+                const bool live = has && g < min(kStageGroups, nvec - st * kStageGroups);
+                const uint4 raw = live ? __ldcg(reinterpret_cast<const uint4 *>(src + col0)) : make_uint4(0, 0, 0, 0);
+                if (consumer) take_group(live, raw, col0, blk_special);
+                __syncwarp();
+                __syncthreads();
+                if (s_count > kCap - kConsumers * G) cut();
+            }
+        }
     }
 
     // E4: columns past the last whole 16-byte group (fewer than G)
     if (warp == 0) {
         const int col = c0 + nvec * G + lane;
-        bool ok = col < c1;
-        float v = 0.0f;
-        if (ok) {
-            if (penal && hist_slot(s_hkey, hbits_n, col) >= 0) ok = false;
-            else v = masked(col) ? -kInf : Elem<TIn>::load1(src, col);
+        uint64_t cv[1];
+        uint32_t vm = 0;
+        if (col < c1 && !(penal && hist_slot(s_hkey, hbits_n, col) >= 0)) {
+            const float v = masked(col) ? -kInf : Elem<TIn>::load1(src, col);
+            if (test(v, col, cv[0])) vm = 1u;
         }
-        consider(ok, v, col);
+        if (__any_sync(0xffffffffu, vm != 0)) append_m(vm, cv, std::integral_constant<int, 1>());
     }
     if (kDebug && a.dbg_processed) {
         float * processed = a.dbg_processed + (int64_t) row * vocab;
         for (int col = c0 + tid; col < c1; col += blockDim.x) {
             const int hs = penal ? hist_slot(s_hkey, hbits_n, col) : -1;
-            processed[col] = hs >= 0 ? __int_as_float(s_hval[hs]) : (masked(col) ? -kInf : Elem<TIn>::load1(src, col));
+            float v = Elem<TIn>::load1(src, col);
+            if (hs >= 0) v = penalize(v, s_hcnt[hs], p);
+            processed[col] = masked(col) ? -kInf : v;
         }
     }
+    __syncwarp();
     __syncthreads();
 
-    // E5: this CTA's best, sorted
-    int nc = s_count;
-    if (nc > 256 && nc > k) {
-        cut();
-        nc = s_count;
+    // E5: this CTA's best min(k, n) candidates, sorted, by rank (composites are distinct)
+    if (s_count > kRankMax) cut();
+    const int nc = s_count;
+    const int kk0 = nc < k ? nc : k;
+    if (tid < nc) {
+        const uint64_t mine = s_cand[tid];
+        int rank = 0;
+        for (int j = 0; j < nc; j++) rank += s_cand[j] > mine;
+        if (rank < kk0) s_sel[rank] = mine;
     }
-    int np2 = 2;
-    while (np2 < nc) np2 <<= 1;
-    for (int i = nc + tid; i < np2; i += blockDim.x) s_cand[i] = 0ull;
-    __syncthreads();
-    bitonic_sort_desc(s_cand, np2);
-    int kk = nc < k ? nc : k;
     const float rmax = block_max_nan(acc, s_redf);
     const int nanf = block_or(nan_scaled, s_redi) | (s_abort ? 2 : 0);
+    int kk = kk0;
 
-    const uint64_t * sorted = s_cand;
     float row_max = rmax;
     int row_flags = nanf;
     if (splits > 1) {
         const int64_t slot = (int64_t) row * splits + split;
-        for (int i = tid; i < kk; i += blockDim.x) sa.part_cand[slot * sa.r.k_bound + i] = s_cand[i];
+        for (int i = tid; i < kk; i += blockDim.x) sa.part_cand[slot * sa.r.k_bound + i] = s_sel[i];
         if (tid == 0) {
             sa.part_n[slot] = kk;
             sa.part_max[slot] = rmax;
@@ -498,8 +563,7 @@ __global__ void __launch_bounds__(kStreamCtaThreads, 2) topk_rows_kernel(const S
         row_flags = block_or(f & 1, s_redi) | (block_or(f & 2, s_redi) ? 2 : 0);
         // each consumer warp merges the lists of splits w, w+8, ...; warp 0 merges the warps' results
         uint64_t * lists = s_cand;  // [kConsumerWarps][32*QN]
-        __syncthreads();
-        if (warp < kConsumerWarps) {
+        if (consumer) {
             uint64_t q[QN];
 #pragma unroll
             for (int r = 0; r < QN; r++) q[r] = 0;
@@ -539,7 +603,6 @@ __global__ void __launch_bounds__(kStreamCtaThreads, 2) topk_rows_kernel(const S
         __syncthreads();
         const int nz = s_n0;
         kk = nz < k ? nz : k;
-        sorted = s_sel;
     }
 
     // ---- finalize the row (one CTA)
@@ -563,15 +626,14 @@ __global__ void __launch_bounds__(kStreamCtaThreads, 2) topk_rows_kernel(const S
     }
     if (greedy_row) {
         if (tid == 0) {
-            *id_out = (int32_t) composite_index(sorted[0]), *st_out = SSB_ROW_OK;
+            *id_out = (int32_t) composite_index(s_sel[0]), *st_out = SSB_ROW_OK;
             if (out.count) *out.count = 1;
             if (out.tokens && out.cap > 0) out.tokens[0] = *id_out, out.weights[0] = 1.0;
         }
         return;
     }
     const double u = a.u ? a.u[row] : 0.0;
-    // scratch for the weights: candidate memory past the sorted list (the split path sorted into s_sel)
-    finalize_draw(sorted, kk, p, u, reinterpret_cast<double *>(s_cand + (splits > 1 ? kConsumerWarps * 32 * QN : np2)), out);
+    finalize_draw(s_sel, kk, p, u, reinterpret_cast<double *>(s_cand), out);  // candidate memory as scratch
 }
 
 template <typename TIn, int KW, bool kDebug>
@@ -593,6 +655,8 @@ void * pick_kernel(int kw, bool bf16, bool debug) {
 
 }  // namespace
 
+int topk_max_chunk(bool bf16) { return kMaxStages * kStageBytes / (bf16 ? 2 : 4); }
+
 size_t topk_smem_bytes(int kw, bool bf16, int chunk, int hist_slots, int sel_slots) {
     const int64_t nst = ((int64_t) chunk * (bf16 ? 2 : 4) + kStageBytes - 1) / kStageBytes;
     const int qn = kw;
@@ -604,7 +668,7 @@ int topk_blocks_per_sm(int kw, bool bf16, size_t smem) {
     void * kern = pick_kernel(kw, bf16, false);
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem) != cudaSuccess) return 0;
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kStreamCtaThreads, smem) != cudaSuccess) return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kTkThreads, smem) != cudaSuccess) return 0;
     return n;
 }
 
@@ -614,7 +678,7 @@ cudaError_t launch_topk(const StreamArgs & a, int kw, bool bf16, bool debug, cud
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
     if (e != cudaSuccess) return e;
     void * args[] = {const_cast<StreamArgs *>(&a)};
-    return cudaLaunchKernel(kern, dim3((unsigned) (a.r.rows * a.splits)), dim3(kStreamCtaThreads), args, smem, stream);
+    return cudaLaunchKernel(kern, dim3((unsigned) (a.r.rows * a.splits)), dim3(kTkThreads), args, smem, stream);
 }
 
 }  // namespace ssb
