@@ -496,4 +496,89 @@ __device__ inline void finalize_draw(const uint64_t * sorted, int k, const RowPa
     }
 }
 
+// Running sums of w[0 .. n) in index order (each the reference's sequential accumulation from 0),
+// written to c[0 .. n); the loads of each block of 8 are issued before its additions. Returns the last.
+__device__ __forceinline__ double running_sums(const double * w, double * c, int n) {
+    double s = 0.0;
+    int i = 0;
+    for (; i + 8 <= n; i += 8) {
+        double v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = w[i + j];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            s = __dadd_rn(s, v[j]);
+            c[i + j] = s;
+        }
+    }
+    for (; i < n; i++) {
+        s = __dadd_rn(s, w[i]);
+        c[i] = s;
+    }
+    return s;
+}
+
+// First i < n with c[i] >= limit (`strict`: > limit), n when none; warp-wide.
+__device__ __forceinline__ int warp_first_reach(const double * c, int n, double limit, bool strict) {
+    const int lane = lane_id();
+    for (int base = 0; base < n; base += 32) {
+        const int i = base + lane;
+        const bool hit = i < n && (strict ? c[i] > limit : c[i] >= limit);
+        const unsigned m = __ballot_sync(0xffffffffu, hit);
+        if (m) return base + __ffs(m) - 1;
+    }
+    return n;
+}
+
+// finalize_draw for one warp (warp-synchronous, no block barrier): the same operations in the same
+// order. Each running sum is computed once, without branches, and the warp finds where it crosses its
+// limit. The kept total of pick() is the top-p running sum at the cut (the same additions, from 0, in
+// the same order). `w` is shared scratch of 2 * k doubles; lane 0 writes the outputs.
+__device__ inline void finalize_draw_warp(const uint64_t * sorted, int k, const RowParams & p, double u, double * w,
+                                          const RowOut & out) {
+    const int lane = lane_id();
+    double * c = w + k;  // running sums
+    const float max_logit = composite_value(sorted[0]);
+    if (!(max_logit > -kInf && max_logit < kInf)) {
+        if (lane == 0) {
+            *out.id = -1;
+            *out.status = SSB_ROW_TEMPERATURE_OVERFLOW;
+            if (out.count) *out.count = 0;
+        }
+        return;
+    }
+    // softmax (qwen3-tts/sampler.cpp:80-87)
+    for (int i = lane; i < k; i += 32) w[i] = exp((double) composite_value(sorted[i]) - (double) max_logit);
+    __syncwarp();
+    double sum = 0.0;
+    if (lane == 0) sum = ordered_sum(w, k);
+    sum = __shfl_sync(0xffffffffu, sum, 0);
+    for (int i = lane; i < k; i += 32) w[i] = __ddiv_rn(w[i], sum);
+    __syncwarp();
+    // top-p cut (:88-99): keep through the first running share >= top_p (all k when none, or top_p >= 1)
+    if (lane == 0) running_sums(w, c, k);
+    __syncwarp();
+    const int at = p.top_p < 1.0f ? warp_first_reach(c, k, (double) p.top_p, false) : k;
+    const int keep = at < k ? at + 1 : k;
+    const double total = c[keep - 1];  // pick()'s total over the kept weights
+    if (out.tokens) {
+        for (int i = lane; i < keep && i < out.cap; i += 32) {
+            out.tokens[i] = (int32_t) composite_index(sorted[i]);
+            out.weights[i] = w[i];
+        }
+    }
+    __syncwarp();
+    // pick() (sampling.cpp:9-19): the renormalized shares in parallel, the first running sum > u
+    for (int i = lane; i < keep - 1; i += 32) w[i] = __ddiv_rn(w[i], total);
+    __syncwarp();
+    if (lane == 0) running_sums(w, c, keep - 1);
+    __syncwarp();
+    const int chosen = warp_first_reach(c, keep - 1, u, true);  // keep - 1 (the last) when none passes
+    if (lane == 0) {
+        *out.id = (int32_t) composite_index(sorted[chosen]);
+        *out.status = SSB_ROW_OK;
+        if (out.count) *out.count = keep;
+    }
+}
+
 }  // namespace ssb

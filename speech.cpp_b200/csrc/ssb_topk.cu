@@ -15,14 +15,15 @@
 // rounded up to bf16 (an upper bound of every logit in it) and keeps its two largest plain block maxima.
 //
 // End phase (short, mostly warp-local).
-//   E1  bound: the lanes' kept maxima are 512 restricted logits of distinct tokens (for fp32 rows the
-//       largest bf16 at or below each); the k-th largest of them by a 16-step bisection on their
-//       order keys is s_b. k tokens reach s_b, so for a positive temperature
+//   E1  bound: the lanes' kept maxima are restricted logits of distinct tokens (for fp32 rows the
+//       largest bf16 at or below each). Each consumer warp sorts its lanes' keys and three rounds of
+//       pairwise merges give their exact k-th largest, s_b. k tokens reach s_b, so for a positive temperature
 //       (which keeps the order) every one of the k best has a scaled logit >= c = fl(s_b / T).
 //   E2  history tokens: penalized (and masked) logits computed now, from the logits the stream has just
 //       brought into L2; candidates if they reach c.
-//   E3  pass 2: the blocks whose maximum can reach c form a list; each lane reads one 16-byte group of
-//       them again (from L2), eight blocks per warp and round. Every element that
+//   E3  pass 2: every lane keeps its best block's logits in registers through the stream; its other
+//       blocks whose maximum can reach c (only when its second best can) form a list, read again
+//       from L2 one 16-byte group per lane, eight blocks per warp and round. Every element that
 //       is not a history token is restricted (-inf where masked), divided by the temperature exactly as
 //       the reference does (qwen3-tts/sampler.cpp:73) and keyed as a composite (value, then lowest
 //       index: the order of qwen3-tts/sampler.cpp:78-79 with haru/sampler.cpp:39's tie-break).
@@ -47,9 +48,10 @@ namespace ssb {
 
 namespace {
 
-constexpr int kTkStages = 4;
+constexpr int kTkStages = 3;
 constexpr int kTkThreads = kStreamCtaThreads;      // 8 consumer warps + the producer warp
-constexpr int kCap = kTkStages * kStageBytes / 8;  // candidate composites the ring's memory holds
+constexpr int kStageArea = kConsumers * 64;                     // staged best blocks: 64 bytes per lane
+constexpr int kCap = (kTkStages * kStageBytes - kStageArea) / 8;  // candidate composites in the ring's memory
 constexpr int kMaxStages = 64;                     // stages of one chunk (a lane's pass-2 mask is 64-bit)
 constexpr int kRankMax = kTkThreads;               // candidates ranked directly (one per thread)
 constexpr int kListMax = 1024;                     // pass-2 blocks listed for the cooperative rounds
@@ -70,6 +72,62 @@ __device__ __forceinline__ int block_word(int gi) {
     const int st = gi / kStageGroups;
     const int t = gi % kConsumers;
     return st * kConsumerWarps + (t >> 5);
+}
+
+// Descending bitonic sort of the 32*R u32 of a warp (element r*32 + lane in x[r]).
+template <int R>
+__device__ __forceinline__ void warp_sort_desc_u32(uint32_t (&x)[R]) {
+    const int lane = lane_id();
+#pragma unroll
+    for (int size = 2; size <= 32 * R; size <<= 1) {
+#pragma unroll
+        for (int j = size >> 1; j > 0; j >>= 1) {
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const int i = r * 32 + lane;
+                const bool desc = (i & size) == 0;
+                if (j >= 32) {
+                    const int rp = r ^ (j >> 5);
+                    if (rp > r) {
+                        const uint32_t a = x[r], b = x[rp];
+                        if ((a < b) == desc) x[r] = b, x[rp] = a;
+                    }
+                } else {
+                    const uint32_t o = __shfl_xor_sync(0xffffffffu, x[r], j);
+                    const bool keep_max = ((lane & j) == 0) == desc;
+                    x[r] = keep_max ? (x[r] > o ? x[r] : o) : (x[r] < o ? x[r] : o);
+                }
+            }
+        }
+    }
+}
+
+// Merges two descending lists of 32*R u32 (q and t), keeping the best 32*R sorted in q.
+template <int R>
+__device__ __forceinline__ void warp_merge_sorted_u32(uint32_t (&q)[R], const uint32_t (&t)[R]) {
+    const int lane = lane_id();
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+        const uint32_t o = __shfl_sync(0xffffffffu, t[R - 1 - r], 31 - lane);
+        q[r] = q[r] > o ? q[r] : o;
+    }
+#pragma unroll
+    for (int j = 16 * R; j > 0; j >>= 1) {
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            if (j >= 32) {
+                const int rp = r ^ (j >> 5);
+                if (rp > r) {
+                    const uint32_t a = q[r], b = q[rp];
+                    if (a < b) q[r] = b, q[rp] = a;
+                }
+            } else {
+                const uint32_t o = __shfl_xor_sync(0xffffffffu, q[r], j);
+                const bool keep_max = (lane & j) == 0;
+                q[r] = keep_max ? (q[r] > o ? q[r] : o) : (q[r] < o ? q[r] : o);
+            }
+        }
+    }
 }
 
 // Slot of history token t in the table, or -1.
@@ -99,8 +157,8 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
     __shared__ float s_redf[32];
     __shared__ int s_redi[32];
     __shared__ int s_count, s_gather, s_abort, s_last, s_n0, s_qn;
+    __shared__ uint32_t s_bound;
     __shared__ int s_qlist[kListMax];
-    __shared__ uint32_t s_keys[2 * kConsumers];  // E1 (not ring memory: a slower warp may still read its last stage)
 
     const int tid = (int) threadIdx.x;
     const int warp = warp_id(), lane = lane_id();
@@ -127,13 +185,16 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
     const int nstages = (nvec + kStageGroups - 1) / kStageGroups;
 
     // ---- shared memory: [ring = candidates once the stream is over] [block maxima, bf16] [special-block bitmap]
-    //                     [hash keys] [hash counts] [selected]
+    //                     [history-column bitmap] [hash keys] [hash counts] [selected]
     const int nst_alloc = (sa.chunk * (int) sizeof(TIn) + kStageBytes - 1) / kStageBytes;
     unsigned char * ring = smem;
     uint64_t * s_cand = reinterpret_cast<uint64_t *>(smem);  // [kCap], once the stream is over
+    uint4 * s_stage = reinterpret_cast<uint4 *>(smem + kCap * 8);  // [kConsumers][4], E3
     uint16_t * s_up = reinterpret_cast<uint16_t *>(smem + kTkStages * kStageBytes);  // [nst_alloc][kConsumers]
     uint32_t * s_bb = reinterpret_cast<uint32_t *>(s_up + nst_alloc * kConsumers);  // [nst_alloc][kConsumerWarps]
-    int32_t * s_hkey = reinterpret_cast<int32_t *>(s_bb + nst_alloc * kConsumerWarps);
+    const int hw_alloc = sa.hist_slots > 0 ? ((((sa.chunk + 31) >> 5) + 3) & ~3) : 0;
+    uint32_t * s_hbits = s_bb + nst_alloc * kConsumerWarps;  // [hw_alloc] history columns of the chunk
+    int32_t * s_hkey = reinterpret_cast<int32_t *>(s_hbits + hw_alloc);
     int32_t * s_hcnt = s_hkey + sa.hist_slots;
     uint64_t * s_sel = reinterpret_cast<uint64_t *>(s_hcnt + sa.hist_slots);  // [max(sel_slots, 32*QN)]
 
@@ -168,39 +229,52 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
     // ---- special blocks (all threads, while the first stages load)
     if (special) {
         for (int i = tid; i < nstages * kConsumerWarps; i += blockDim.x) s_bb[i] = 0;
-        if (penal)
+        if (penal) {
             for (int i = tid; i < sa.hist_slots; i += blockDim.x) s_hkey[i] = -1, s_hcnt[i] = 0;
+            for (int i = tid; i < ((sa.chunk + 31) >> 5); i += blockDim.x) s_hbits[i] = 0;
+        }
         __syncthreads();
         if (penal) {
+            // the first occurrence of an id (its column bit was clear) inserts it into the table; then
+            // every occurrence counts itself
             const uint32_t hmask = (uint32_t) sa.hist_slots - 1u;
-            for (int base = 0; base < hlen; base += 4 * kTkThreads) {  // warp-uniform trip count
+            for (int base = 0; base < hlen; base += 4 * kTkThreads) {  // uniform trip count
                 int32_t t[4];
 #pragma unroll
                 for (int q = 0; q < 4; q++) {  // four independent loads in flight
                     const int i = base + q * kTkThreads + tid;
                     t[q] = i < hlen ? __ldg(hist + i) : -1;
                 }
+                bool first[4];
 #pragma unroll
                 for (int q = 0; q < 4; q++) {
-                    const bool in = t[q] >= c0 && t[q] < c1;
-                    const unsigned m = __ballot_sync(0xffffffffu, in);
-                    if (in) {
-                        const unsigned peers = __match_any_sync(m, t[q]);  // duplicates within the warp
-                        if (lane == __ffs(peers) - 1) {
-                            uint32_t h = hash_token(t[q], hbits_n);
-                            for (uint32_t n = 0; n <= hmask; n++) {
-                                const int32_t old = atomicCAS(&s_hkey[h], -1, t[q]);
-                                if (old == -1 || old == t[q]) {
-                                    atomicAdd(&s_hcnt[h], __popc(peers));
-                                    break;
-                                }
-                                h = (h + 1) & hmask;
-                            }
-                            const int gi = (t[q] - c0) / G;
-                            if (gi < nvec) atomicOr(&s_bb[block_word(gi)], 1u << (gi & 31));
-                        }
+                    first[q] = false;
+                    if (t[q] >= c0 && t[q] < c1) {
+                        const int rel = t[q] - c0;
+                        const uint32_t bit = 1u << (rel & 31);
+                        first[q] = !(atomicOr(&s_hbits[rel >> 5], bit) & bit);
                     }
-                    __syncwarp();
+                }
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    if (first[q]) {
+                        uint32_t h = hash_token(t[q], hbits_n);
+                        for (uint32_t n = 0; n <= hmask; n++) {  // distinct keys: only empty slots are taken
+                            if (atomicCAS(&s_hkey[h], -1, t[q]) == -1) break;
+                            h = (h + 1) & hmask;
+                        }
+                        const int gi = (t[q] - c0) / G;
+                        if (gi < nvec) atomicOr(&s_bb[block_word(gi)], 1u << (gi & 31));
+                    }
+                }
+            }
+            __syncthreads();
+            for (int base = 0; base < hlen; base += 4 * kTkThreads) {
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const int i = base + q * kTkThreads + tid;
+                    const int32_t t = i < hlen ? __ldg(hist + i) : -1;
+                    if (t >= c0 && t < c1) atomicAdd(&s_hcnt[hist_slot(s_hkey, hbits_n, t)], 1);
                 }
             }
         }
@@ -246,6 +320,12 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
 
     // ---- pass 1
     uint32_t key0 = 0, key1 = 0;  // the lane's two largest plain block maxima (16-bit order keys; 0: none)
+    // the lane's best block (largest maximum, NaN first) with its logits, and the second largest maximum
+    float best_v = -kInf, second_v = -kInf;
+    int best_st = -1;
+    uint4 best_rv[kGroupsPerThread];
+#pragma unroll
+    for (int j = 0; j < kGroupsPerThread; j++) best_rv[j] = make_uint4(0, 0, 0, 0);
     if (!consumer) {
         // producer
         if (lane == 0) {
@@ -286,28 +366,52 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
                 key1 = kb > key0 ? key0 : kb;
                 key0 = kb > key0 ? kb : key0;
             }
+            const float bv = lm == lm ? lm : kInf;
+            if (best_st < 0 || bv > best_v) {
+                second_v = best_st < 0 ? -kInf : best_v;
+                best_v = bv;
+                best_st = st;
+#pragma unroll
+                for (int j = 0; j < kGroupsPerThread; j++) best_rv[j] = rv[j];
+            } else if (bv > second_v) {
+                second_v = bv;
+            }
         }
     }
     __syncwarp();
 
     // ---- end phase (all threads)
-    if (consumer) s_keys[tid] = key0, s_keys[kConsumers + tid] = key1;
+    // E1: the exact k-th largest of the lanes' kept keys: each consumer warp sorts its 64, then three
+    // rounds of pairwise merges keep the best 32*KW (ring memory: every warp is past pass 1 after the
+    // first barrier)
+    uint32_t * s_lists = reinterpret_cast<uint32_t *>(smem);  // [kConsumerWarps][32 * QN]
     __syncthreads();
-    // E1: the largest 16-bit key P that at least k of the 512 reach (every warp computes it)
-    uint32_t P = 0;
-    {
-        uint32_t kv[2 * kConsumers / 32];
+    if (consumer) {
+        uint32_t x[2] = {key0, key1};
+        warp_sort_desc_u32<2>(x);
 #pragma unroll
-        for (int q = 0; q < 2 * kConsumers / 32; q++) kv[q] = s_keys[q * 32 + lane];
-#pragma unroll 1
-        for (int b = 15; b >= 0; b--) {
-            const uint32_t cand = P | (1u << b);
-            uint32_t n = 0;
-#pragma unroll
-            for (int q = 0; q < 2 * kConsumers / 32; q++) n += kv[q] >= cand;
-            if (__reduce_add_sync(0xffffffffu, n) >= (uint32_t) k) P = cand;
-        }
+        for (int r = 0; r < QN; r++) s_lists[warp * 32 * QN + r * 32 + lane] = r < 2 ? x[r < 2 ? r : 0] : 0u;
     }
+    __syncthreads();
+#pragma unroll 1
+    for (int step = 1; step < kConsumerWarps; step <<= 1) {
+        if (consumer && (warp & (2 * step - 1)) == 0) {
+            uint32_t q[QN], t[QN];
+#pragma unroll
+            for (int r = 0; r < QN; r++) {
+                q[r] = s_lists[warp * 32 * QN + r * 32 + lane];
+                t[r] = s_lists[(warp + step) * 32 * QN + r * 32 + lane];
+            }
+            warp_merge_sorted_u32<QN>(q, t);
+            __syncwarp();
+#pragma unroll
+            for (int r = 0; r < QN; r++) s_lists[warp * 32 * QN + r * 32 + lane] = q[r];
+        }
+        __syncthreads();
+    }
+    if (tid == 0) s_bound = s_lists[k - 1];
+    __syncthreads();  // s_lists is ring memory, about to hold candidates
+    const uint32_t P = s_bound;
     // P <= key of -inf (no k keys): no bound; else the value of key P << 16 is at or below k restricted
     // logits
     const float s_b = (P << 16) <= order_key(-kInf) ? -kInf : key_value(P << 16);
@@ -354,30 +458,35 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
         for (int i = 0; i < N; i++)
             if ((vm >> i) & 1u) s_cand[base + __popc(vm & ((1u << i) - 1u))] = cv[i];
     };
-    // restricted logit v of column col: statistics, and whether its composite reaches theta
+    // restricted logit v of column col: whether its composite reaches theta
     auto test = [&](float v, int col, uint64_t & cv) {
-        acc = max_nan(acc, v);
         if (!(v >= rb)) return false;
         const float sc = scale ? __fdiv_rn(v, T) : v;
         nan_scaled |= sc != sc;
         cv = composite(sc, (uint32_t) col);
         return cv >= theta;
     };
-    // one 16-byte group of restricted-candidate elements (history elements are skipped: taken in E2)
+    // one 16-byte group: its restricted logits into the maximum, its candidates appended (history elements
+    // are skipped: taken in E2). A plain group below the raw bound has no candidate.
     auto take_group = [&](bool live, const uint4 & raw, int col0, bool blk_special) {
         uint64_t cv[G];
         uint32_t vm = 0;
         if (live) {
-            float v[G];
-            Elem<TIn>::unpack(raw, v);
+            const float gm = group_max<TIn>(raw);
+            if (!blk_special) acc = max_nan(acc, gm);
+            if (blk_special || gm >= rb) {
+                float v[G];
+                Elem<TIn>::unpack(raw, v);
 #pragma unroll
-            for (int e = 0; e < G; e++) {
-                bool skip = false;
-                if (blk_special) {
-                    if (penal && hist_slot(s_hkey, hbits_n, col0 + e) >= 0) skip = true;
-                    else if (masked(col0 + e)) v[e] = -kInf;
+                for (int e = 0; e < G; e++) {
+                    bool skip = false;
+                    if (blk_special) {
+                        if (penal && ((s_hbits[(col0 + e - c0) >> 5] >> ((col0 + e - c0) & 31)) & 1u)) skip = true;
+                        else if (masked(col0 + e)) v[e] = -kInf;
+                        if (!skip) acc = max_nan(acc, v[e]);
+                    }
+                    if (!skip && test(v[e], col0 + e, cv[e])) vm |= 1u << e;
                 }
-                if (!skip && test(v[e], col0 + e, cv[e])) vm |= 1u << e;
             }
         }
         if (__any_sync(0xffffffffu, vm != 0)) append_m(vm, cv, std::integral_constant<int, G>());
@@ -420,6 +529,7 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
                 if (t[q] >= 0) {
                     const int i = base + q * kTkThreads + tid;
                     const float v = masked(t[q]) ? -kInf : penalize(raw[q], s_hcnt[i], p);
+                    acc = max_nan(acc, v);
                     if (test(v, t[q], cv[q])) vm |= 1u << q;
                 }
             }
@@ -430,16 +540,26 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
         }
     }
 
-    // E3: pass 2 over the blocks whose maximum can reach the threshold
-    uint64_t qmask = 0;  // stages of this lane's qualifying blocks
-    if (consumer)
+    // E3: pass 2 over the blocks whose maximum can reach the threshold. A lane's best block is still in
+    // its registers: it is staged in shared memory; its other qualifying blocks (only when its second
+    // best can qualify) are read again from L2. All of them are listed and taken cooperatively, one
+    // 16-byte group per lane, eight blocks per warp and round.
+    const bool best_q = consumer && best_st >= 0 && qualifies(best_v);
+    uint64_t qmask = 0;  // stages of this lane's other qualifying blocks
+    if (best_q && qualifies(second_v))
         for (int st = 0; st < nstages; st++)
-            if (qualifies(__uint_as_float((uint32_t) s_up[st * kConsumers + tid] << 16))) qmask |= 1ull << st;
+            if (st != best_st && qualifies(__uint_as_float((uint32_t) s_up[st * kConsumers + tid] << 16))) qmask |= 1ull << st;
     const int nq = __popcll(qmask);
-    if (nq > 0) {
-        const int at = atomicAdd(&s_qn, nq);
+    if (best_q) {
+#pragma unroll
+        for (int j = 0; j < kGroupsPerThread; j++) s_stage[tid * kGroupsPerThread + j] = best_rv[j];
+    }
+    if (best_q || nq > 0) {
+        const int at = atomicAdd(&s_qn, nq + (best_q ? 1 : 0));
+        int i = 0;
+        if (best_q && at < kListMax) s_qlist[at] = (1 << 30) | (best_st << 9) | tid, i = 1;  // bit 30: staged
         uint64_t m = qmask;
-        for (int i = 0; i < nq && at + i < kListMax; i++) {
+        for (; i < nq + (best_q ? 1 : 0) && at + i < kListMax; i++) {
             const int st = __ffsll((long long) m) - 1;
             m &= m - 1;
             s_qlist[at + i] = (st << 9) | tid;
@@ -451,7 +571,6 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
     const bool synced = s_count + qtotal * kBlockElems + G > kCap;
     if (synced && s_count > kCap - kConsumers * G) cut();
     if (qtotal <= kListMax) {
-        // cooperative rounds: a consumer warp takes eight listed blocks, lane l group l & 3 of block l >> 2
         const int rounds = (qtotal + kRoundBlocks - 1) / kRoundBlocks;
         for (int r = 0; r < rounds; r++) {  // CTA-uniform
             if (consumer) {
@@ -463,11 +582,11 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
                 bool blk_special = false;
                 if (e < qtotal) {
                     const int ent = s_qlist[e];
-                    const int st = ent >> 9, t = ent & 511;
+                    const int st = (ent >> 9) & 0x1FFFF, t = ent & 511;
                     const int g = j * kConsumers + t;
                     col0 = c0 + st * kStageElems + g * G;
                     live = g < min(kStageGroups, nvec - st * kStageGroups);
-                    if (live) raw = __ldcg(reinterpret_cast<const uint4 *>(src + col0));
+                    if (live) raw = (ent >> 30) ? s_stage[t * kGroupsPerThread + j] : __ldcg(reinterpret_cast<const uint4 *>(src + col0));
                     blk_special = special && ((s_bb[st * kConsumerWarps + (t >> 5)] >> (t & 31)) & 1u);
                 }
                 take_group(live, raw, col0, blk_special);
@@ -480,7 +599,8 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
         }
     } else {
         // a list that long (no useful bound): each lane takes its own blocks, one group per round
-        const int passes = block_max_int(nq, s_redi);
+        if (best_q) qmask |= 1ull << best_st;
+        const int passes = block_max_int(__popcll(qmask), s_redi);
         for (int pass = 0; pass < passes; pass++) {  // CTA-uniform
             const bool has = qmask != 0;
             const int st = has ? __ffsll((long long) qmask) - 1 : 0;
@@ -504,8 +624,9 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
         const int col = c0 + nvec * G + lane;
         uint64_t cv[1];
         uint32_t vm = 0;
-        if (col < c1 && !(penal && hist_slot(s_hkey, hbits_n, col) >= 0)) {
+        if (col < c1 && !(penal && ((s_hbits[(col - c0) >> 5] >> ((col - c0) & 31)) & 1u))) {
             const float v = masked(col) ? -kInf : Elem<TIn>::load1(src, col);
+            acc = max_nan(acc, v);
             if (test(v, col, cv[0])) vm = 1u;
         }
         if (__any_sync(0xffffffffu, vm != 0)) append_m(vm, cv, std::integral_constant<int, 1>());
@@ -633,7 +754,7 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
         return;
     }
     const double u = a.u ? a.u[row] : 0.0;
-    finalize_draw(s_sel, kk, p, u, reinterpret_cast<double *>(s_cand), out);  // candidate memory as scratch
+    if (warp == 0) finalize_draw_warp(s_sel, kk, p, u, reinterpret_cast<double *>(s_cand), out);  // candidate memory as scratch
 }
 
 template <typename TIn, int KW, bool kDebug>
@@ -660,8 +781,9 @@ int topk_max_chunk(bool bf16) { return kMaxStages * kStageBytes / (bf16 ? 2 : 4)
 size_t topk_smem_bytes(int kw, bool bf16, int chunk, int hist_slots, int sel_slots) {
     const int64_t nst = ((int64_t) chunk * (bf16 ? 2 : 4) + kStageBytes - 1) / kStageBytes;
     const int qn = kw;
+    const size_t hwords = hist_slots > 0 ? (size_t) ((((chunk + 31) >> 5) + 3) & ~3) : 0;
     return (size_t) kTkStages * kStageBytes + (size_t) nst * kConsumers * 2 + (size_t) nst * kConsumerWarps * 4 +
-           (size_t) hist_slots * 8 + (size_t) (sel_slots > 32 * qn ? sel_slots : 32 * qn) * 8;
+           hwords * 4 + (size_t) hist_slots * 8 + (size_t) (sel_slots > 32 * qn ? sel_slots : 32 * qn) * 8;
 }
 
 int topk_blocks_per_sm(int kw, bool bf16, size_t smem) {
