@@ -53,6 +53,8 @@ def parse_args():
     ap.add_argument("--density", type=float, default=0.01, help="config 5 allow-mask density")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--launches-only", type=int, default=0,
+                    help="profiling aid: after the oracle check, issue this many launches and exit (no timing, no JSON)")
     return ap.parse_args()
 
 
@@ -260,6 +262,15 @@ def main():
             print(json.dumps({"error": "engine ids differ from the oracle", "got": got.tolist(), "want": want.tolist()}),
                   file=sys.stderr)
 
+    if args.launches_only:
+        with torch.cuda.stream(stream):
+            for i in range(args.launches_only):
+                launch(i % pool_n, stream)
+        stream.synchronize()
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
     # capture one launch per pool batch into a CUDA graph
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.stream(stream):
@@ -355,7 +366,7 @@ def main():
             try:
                 tj = json.load(open(tf))
                 key = f"config{args.config}_rows{rows}"
-                traffic = tj.get(key)
+                traffic = (tj.get(key) or {}).get("dram_bytes_per_launch")
             except Exception:
                 traffic = None
         cpu = None
@@ -383,7 +394,7 @@ def main():
                              "cycled by CUDA-graph replay", "parallelism": f"batch-partitioned x{world}, no collective",
                        "oracle_check_rows_equal": check},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "traffic": traffic, "peak_kind": peak_kind,
+                         "traffic": traffic, "traffic_unit": "bytes per launch (ncu dram read + write, profiles/traffic.json)", "peak_kind": peak_kind,
                          "algorithmic_bytes_per_launch": bytes_per_launch,
                          "note": "logits bytes read per launch / average launch time (graph-replayed back to back)"},
             "cpu_baseline": cpu,
