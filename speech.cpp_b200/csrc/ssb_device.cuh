@@ -403,141 +403,47 @@ struct RowOut {
     int cap;
 };
 
-// Sum of w[0 .. n) added in index order (the reference's sequential accumulation); the loads of each
-// block of 8 are issued before its additions.
-__device__ __forceinline__ double ordered_sum(const double * w, int n) {
+// The running sum of w[0 .. n) in index order (the reference's sequential accumulation from 0), one
+// thread: the first index at which it reaches `limit` (`strict`: exceeds it) or n, with the sum there
+// (or over all n) in *at_sum. `limit` = +inf gives the plain ordered sum. The next 8 values load while
+// the current 8 are added, so the chain runs at the latency of the additions.
+__device__ __forceinline__ int chain_reach(const double * w, int n, double limit, bool strict, double * at_sum) {
     double s = 0.0;
-    int i = 0;
-    for (; i + 8 <= n; i += 8) {
-        double v[8];
+    int at = n;
+    double cur[8], nxt[8];
 #pragma unroll
-        for (int j = 0; j < 8; j++) v[j] = w[i + j];
-#pragma unroll
-        for (int j = 0; j < 8; j++) s = __dadd_rn(s, v[j]);
-    }
-    for (; i < n; i++) s = __dadd_rn(s, w[i]);
-    return s;
-}
-
-// Index of the first i < n at which the running sum of w[0 .. i] (in index order) passes the limit
-// (`strict`: > limit, else >= limit); n when it never does.
-__device__ __forceinline__ int first_crossing(const double * w, int n, double limit, bool strict) {
-    double s = 0.0;
+    for (int j = 0; j < 8; j++) cur[j] = j < n ? w[j] : 0.0;
     for (int i = 0; i < n; i += 8) {
-        double v[8];
 #pragma unroll
-        for (int j = 0; j < 8; j++) v[j] = i + j < n ? w[i + j] : 0.0;
+        for (int j = 0; j < 8; j++) nxt[j] = i + 8 + j < n ? w[i + 8 + j] : 0.0;
+        bool done = false;
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-            if (i + j < n) {
-                s = __dadd_rn(s, v[j]);
-                if (strict ? s > limit : s >= limit) return i + j;
+            if (!done && i + j < n) {
+                s = __dadd_rn(s, cur[j]);
+                if (strict ? s > limit : s >= limit) {
+                    at = i + j;
+                    done = true;
+                }
             }
         }
-    }
-    return n;
-}
-
-// The reference's softmax, top-p and pick over the k candidates sorted by composite (descending):
-// weights exp((double)s - max) summed in order (qwen3-tts/sampler.cpp:85-87), normalized, cut at the
-// first cumulative share >= top_p (:88-99), then pick() (sampling.cpp:9-19): each a sequence of
-// IEEE double operations in the reference's order, so the same values come out. `w` is shared
-// scratch of k doubles. Block-wide; thread 0 writes the outputs.
-__device__ inline void finalize_draw(const uint64_t * sorted, int k, const RowParams & p, double u, double * w,
-                              const RowOut & out) {
-    const float max_logit = composite_value(sorted[0]);
-    const bool overflow = !(max_logit > -kInf && max_logit < kInf);
-    if (overflow) {
-        if (threadIdx.x == 0) {
-            *out.id = -1;
-            *out.status = SSB_ROW_TEMPERATURE_OVERFLOW;
-            if (out.count) *out.count = 0;
-        }
-        return;
-    }
-    __shared__ double s_sum;
-    __shared__ int s_keep;
-    // softmax (qwen3-tts/sampler.cpp:80-87): exp of the shifted logits in parallel, their sum in order
-    for (int i = threadIdx.x; i < k; i += blockDim.x) w[i] = exp((double) composite_value(sorted[i]) - (double) max_logit);
-    __syncthreads();
-    if (threadIdx.x == 0) s_sum = ordered_sum(w, k);
-    __syncthreads();
-    const double sum = s_sum;
-    for (int i = threadIdx.x; i < k; i += blockDim.x) w[i] = __ddiv_rn(w[i], sum);
-    __syncthreads();
-    // top-p cut (:88-99): keep through the first cumulative share >= top_p; then pick()'s total
-    if (threadIdx.x == 0) {
-        int keep = k;
-        if (p.top_p < 1.0f) {
-            const int at = first_crossing(w, k, (double) p.top_p, false);
-            keep = at < k ? at + 1 : k;
-        }
-        s_keep = keep;
-        s_sum = ordered_sum(w, keep);
-    }
-    __syncthreads();
-    const int keep = s_keep;
-    const double s2 = s_sum;
-    if (out.tokens) {
-        for (int i = threadIdx.x; i < keep && i < out.cap; i += blockDim.x) {
-            out.tokens[i] = (int32_t) composite_index(sorted[i]);
-            out.weights[i] = w[i];
-        }
-        __syncthreads();
-    }
-    // pick() (sampling.cpp:9-19): the renormalized shares in parallel, the first cumulative > u in order
-    for (int i = threadIdx.x; i < keep - 1; i += blockDim.x) w[i] = __ddiv_rn(w[i], s2);
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const int chosen = first_crossing(w, keep - 1, u, true);  // keep - 1 (the last) when none passes
-        *out.id = (int32_t) composite_index(sorted[chosen]);
-        *out.status = SSB_ROW_OK;
-        if (out.count) *out.count = keep;
-    }
-}
-
-// Running sums of w[0 .. n) in index order (each the reference's sequential accumulation from 0),
-// written to c[0 .. n); the loads of each block of 8 are issued before its additions. Returns the last.
-__device__ __forceinline__ double running_sums(const double * w, double * c, int n) {
-    double s = 0.0;
-    int i = 0;
-    for (; i + 8 <= n; i += 8) {
-        double v[8];
+        if (done) break;
 #pragma unroll
-        for (int j = 0; j < 8; j++) v[j] = w[i + j];
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            s = __dadd_rn(s, v[j]);
-            c[i + j] = s;
-        }
+        for (int j = 0; j < 8; j++) cur[j] = nxt[j];
     }
-    for (; i < n; i++) {
-        s = __dadd_rn(s, w[i]);
-        c[i] = s;
-    }
-    return s;
+    *at_sum = s;
+    return at;
 }
 
-// First i < n with c[i] >= limit (`strict`: > limit), n when none; warp-wide.
-__device__ __forceinline__ int warp_first_reach(const double * c, int n, double limit, bool strict) {
-    const int lane = lane_id();
-    for (int base = 0; base < n; base += 32) {
-        const int i = base + lane;
-        const bool hit = i < n && (strict ? c[i] > limit : c[i] >= limit);
-        const unsigned m = __ballot_sync(0xffffffffu, hit);
-        if (m) return base + __ffs(m) - 1;
-    }
-    return n;
-}
-
-// finalize_draw for one warp (warp-synchronous, no block barrier): the same operations in the same
-// order. Each running sum is computed once, without branches, and the warp finds where it crosses its
-// limit. The kept total of pick() is the top-p running sum at the cut (the same additions, from 0, in
-// the same order). `w` is shared scratch of 2 * k doubles; lane 0 writes the outputs.
+// The draw of one row by one warp (warp-synchronous, no block barrier): the reference's softmax, top-p
+// cut and pick() over the k candidates sorted by composite (descending), as IEEE double operations in
+// the reference's order (qwen3-tts/sampler.cpp:80-99, sampling.cpp:9-19). The parallel steps (exp, the divisions) run across the lanes with all of a lane's operations
+// issued together; the three running sums (the softmax total, the top-p cut, pick()) run on lane 0. The
+// kept total of pick() is the top-p running sum at the cut (the same additions, from 0, in the same
+// order). `w` is shared scratch of k doubles; lane 0 writes the outputs.
 __device__ inline void finalize_draw_warp(const uint64_t * sorted, int k, const RowParams & p, double u, double * w,
                                           const RowOut & out) {
     const int lane = lane_id();
-    double * c = w + k;  // running sums
     const float max_logit = composite_value(sorted[0]);
     if (!(max_logit > -kInf && max_logit < kInf)) {
         if (lane == 0) {
@@ -548,19 +454,43 @@ __device__ inline void finalize_draw_warp(const uint64_t * sorted, int k, const 
         return;
     }
     // softmax (qwen3-tts/sampler.cpp:80-87)
-    for (int i = lane; i < k; i += 32) w[i] = exp((double) composite_value(sorted[i]) - (double) max_logit);
+    for (int base = 0; base < k; base += 128) {
+        double e[4];
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            const int i = base + lane + 32 * r;
+            e[r] = i < k ? exp((double) composite_value(sorted[i]) - (double) max_logit) : 0.0;
+        }
+#pragma unroll
+        for (int r = 0; r < 4; r++)
+            if (base + lane + 32 * r < k) w[base + lane + 32 * r] = e[r];
+    }
     __syncwarp();
     double sum = 0.0;
-    if (lane == 0) sum = ordered_sum(w, k);
+    if (lane == 0) chain_reach(w, k, kInf, true, &sum);
     sum = __shfl_sync(0xffffffffu, sum, 0);
-    for (int i = lane; i < k; i += 32) w[i] = __ddiv_rn(w[i], sum);
+    for (int base = 0; base < k; base += 128) {
+        double q[4];
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            const int i = base + lane + 32 * r;
+            q[r] = i < k ? __ddiv_rn(w[i], sum) : 0.0;
+        }
+#pragma unroll
+        for (int r = 0; r < 4; r++)
+            if (base + lane + 32 * r < k) w[base + lane + 32 * r] = q[r];
+    }
     __syncwarp();
-    // top-p cut (:88-99): keep through the first running share >= top_p (all k when none, or top_p >= 1)
-    if (lane == 0) running_sums(w, c, k);
-    __syncwarp();
-    const int at = p.top_p < 1.0f ? warp_first_reach(c, k, (double) p.top_p, false) : k;
-    const int keep = at < k ? at + 1 : k;
-    const double total = c[keep - 1];  // pick()'s total over the kept weights
+    // top-p cut (:88-99): keep through the first running share >= top_p (all k when none, or top_p >= 1);
+    // the running sum there is pick()'s total over the kept weights
+    int keep = k;
+    double total = 0.0;
+    if (lane == 0) {
+        const int at = chain_reach(w, k, p.top_p < 1.0f ? (double) p.top_p : kInf, false, &total);
+        keep = at < k ? at + 1 : k;
+    }
+    keep = __shfl_sync(0xffffffffu, keep, 0);
+    total = __shfl_sync(0xffffffffu, total, 0);
     if (out.tokens) {
         for (int i = lane; i < keep && i < out.cap; i += 32) {
             out.tokens[i] = (int32_t) composite_index(sorted[i]);
@@ -568,13 +498,22 @@ __device__ inline void finalize_draw_warp(const uint64_t * sorted, int k, const 
         }
     }
     __syncwarp();
-    // pick() (sampling.cpp:9-19): the renormalized shares in parallel, the first running sum > u
-    for (int i = lane; i < keep - 1; i += 32) w[i] = __ddiv_rn(w[i], total);
+    // pick() (sampling.cpp:9-19): the renormalized shares, then the first running sum > u (else the last)
+    for (int base = 0; base < keep - 1; base += 128) {
+        double q[4];
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            const int i = base + lane + 32 * r;
+            q[r] = i < keep - 1 ? __ddiv_rn(w[i], total) : 0.0;
+        }
+#pragma unroll
+        for (int r = 0; r < 4; r++)
+            if (base + lane + 32 * r < keep - 1) w[base + lane + 32 * r] = q[r];
+    }
     __syncwarp();
-    if (lane == 0) running_sums(w, c, keep - 1);
-    __syncwarp();
-    const int chosen = warp_first_reach(c, keep - 1, u, true);  // keep - 1 (the last) when none passes
     if (lane == 0) {
+        double unused;
+        const int chosen = chain_reach(w, keep - 1, u, true, &unused);  // keep - 1 (the last) when none passes
         *out.id = (int32_t) composite_index(sorted[chosen]);
         *out.status = SSB_ROW_OK;
         if (out.count) *out.count = keep;

@@ -31,7 +31,7 @@
 //       blocks could overflow it (or the list), the rounds are synchronized and the array is cut to
 //       its k best by a radix select (which also raises the threshold) between them.
 //   E4  columns past the last whole 16-byte group.
-//   E5  the candidates are ranked (each against all: they are few and distinct), and finalize_draw
+//   E5  the candidates are ranked (each against all: they are few and distinct), and finalize_draw_warp
 //       replays the reference's double-precision softmax, top-p cut and pick.
 // The restricted maximum (for the row statuses, qwen3-tts/sampler.cpp:43-49) is exact: the largest
 // restricted logit lies in a block whose maximum reaches c, or is a history token.
