@@ -25,6 +25,9 @@ struct ssb_context {
     float * part_max = nullptr;      // [max_slots]
     int32_t * part_flags = nullptr;  // [max_slots]
     uint32_t * counters = nullptr;   // [max_slots]
+    // rows that keep more than kStreamMaxK tokens: one region of the list per resident CTA, grown on use
+    uint64_t * nuc_scratch = nullptr;
+    size_t nuc_bytes = 0;
     // host-call staging
     unsigned char * stage = nullptr;
     size_t stage_bytes = 0;
@@ -70,7 +73,7 @@ ssb_status use_device(const ssb_context * ctx) {
 int64_t div_up(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 struct Plan {
-    int kernel;  // 0 small, 1 stream
+    int kernel;  // 0 small, 1 stream (select / top-k / stream kernels), 2 nucleus (top-k above kStreamMaxK)
     int mode;    // stream: 0 greedy, 1 top-k
     int k_bound;
 };
@@ -115,9 +118,7 @@ ssb_status check_rows(const ssb_rows * r, bool device_side, Plan * plan) {
         return fail(SSB_OUT_OF_RANGE, "history_ld exceeds SSB_MAX_STREAM_HISTORY (8192) for a vocabulary of more than 8192 tokens");
     plan->kernel = 1;
     plan->mode = all_greedy ? 0 : 1;
-    if (plan->mode == 1 && kb > ssb::kStreamMaxK)
-        return fail(SSB_OUT_OF_RANGE, "a top-k above 1024 (or 0 = every token) over a vocabulary of more than 8192 tokens "
-                                      "is not supported by this build");
+    if (plan->mode == 1 && kb > ssb::kStreamMaxK) plan->kernel = 2;
     (void) device_side;
     return SSB_OK;
 }
@@ -173,6 +174,31 @@ ssb_status run(ssb_context * ctx, const ssb_rows * r, const Debug * dbg, cudaStr
     if (plan.kernel == 0) {
         e = ssb::launch_small(a, bf16, debug, stream);
         if (e != cudaSuccess) return cuda_fail(e, "small-row kernel launch");
+        return ok();
+    }
+    if (plan.kernel == 2) {
+        ssb::NucleusArgs na{};
+        na.r = a;
+        na.r.k_bound = plan.k_bound;
+        na.hist_slots = r->history ? ssb::next_pow2((int) std::max<int64_t>(4, 2 * r->history_ld)) : 0;
+        const size_t smem = ssb::nucleus_smem_bytes(r->vocab, na.hist_slots);
+        if (smem > (size_t) ctx->max_smem) return fail(SSB_OUT_OF_RANGE, "the history and vocabulary need more shared memory than the device has");
+        const int occ = ssb::nucleus_blocks_per_sm(bf16, smem);
+        if (occ <= 0) return fail(SSB_DEVICE, "the nucleus kernel does not fit on this device");
+        const int grid = std::min(r->rows, ctx->sm_count * occ);
+        na.scratch_ld = ssb::nucleus_scratch_ld(r->vocab);
+        const size_t need = (size_t) grid * (size_t) na.scratch_ld * sizeof(uint64_t);
+        if (need > ctx->nuc_bytes) {
+            cudaFree(ctx->nuc_scratch);
+            ctx->nuc_scratch = nullptr;
+            ctx->nuc_bytes = 0;
+            e = cudaMalloc(&ctx->nuc_scratch, need);
+            if (e != cudaSuccess) return cuda_fail(e, "nucleus scratch");
+            ctx->nuc_bytes = need;
+        }
+        na.scratch = ctx->nuc_scratch;
+        e = ssb::launch_nucleus(na, grid, bf16, debug, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "nucleus kernel launch");
         return ok();
     }
     const int mode = plan.mode;
@@ -314,6 +340,7 @@ ssb_status ssb_context_destroy(ssb_context * ctx) {
     cudaFree(ctx->part_flags);
     cudaFree(ctx->counters);
     cudaFree(ctx->stage);
+    cudaFree(ctx->nuc_scratch);
     if (ctx->done) cudaEventDestroy(ctx->done);
     if (cur >= 0) cudaSetDevice(cur);
     delete ctx;

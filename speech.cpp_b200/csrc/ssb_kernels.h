@@ -80,4 +80,19 @@ size_t topk_smem_bytes(int kw, bool bf16, int chunk, int hist_slots, int sel_slo
 int topk_blocks_per_sm(int kw, bool bf16, size_t smem);
 cudaError_t launch_topk(const StreamArgs & a, int kw, bool bf16, bool debug, cudaStream_t stream);
 
+// Rows whose top-k keeps more than kStreamMaxK tokens (top-k 0 = all) over a large vocabulary
+// (ssb_nucleus.cu): one CTA per row at a time (rows looped over the grid), each with its own region of
+// `scratch` (scratch_ld composites) for the row's finite scaled logits.
+struct NucleusArgs {
+    RowsArgs r;
+    uint64_t * scratch;
+    int64_t scratch_ld;
+    int hist_slots;
+};
+size_t nucleus_smem_bytes(int vocab, int hist_slots);
+int64_t nucleus_scratch_ld(int vocab);
+int nucleus_threads();
+int nucleus_blocks_per_sm(bool bf16, size_t smem);
+cudaError_t launch_nucleus(const NucleusArgs & a, int grid, bool bf16, bool debug, cudaStream_t stream);
+
 }  // namespace ssb

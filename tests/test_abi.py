@@ -76,8 +76,9 @@ def test_semantic_refusals(lib):
     assert "u is required" in lib.ssb_last_error().decode()
     r = _rows(mask_kind=ss.MASK_BAN)  # a mask kind without a mask
     assert lib.ssb_sample_rows(None, ctypes.byref(r), None) == ss.INVALID_ARGUMENT
-    r = _rows(vocab=151936, ld=151936, params=ss.params(top_k=0), u=0x4000)  # k above the streaming limit
-    assert lib.ssb_sample_rows(None, ctypes.byref(r), None) in (ss.OUT_OF_RANGE, ss.INVALID_ARGUMENT)
+    r = _rows(vocab=151936, ld=151936, params=ss.params(top_k=0), u=0x4000)  # every token kept: valid, no ctx
+    assert lib.ssb_sample_rows(None, ctypes.byref(r), None) == ss.INVALID_ARGUMENT
+    assert "ctx" in lib.ssb_last_error().decode()
     r = _rows(vocab=151936, ld=151936, history=0x5000, history_ld=9000)
     assert lib.ssb_sample_rows(None, ctypes.byref(r), None) == ss.OUT_OF_RANGE
     assert "SSB_MAX_STREAM_HISTORY" in lib.ssb_last_error().decode()

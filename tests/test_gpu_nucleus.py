@@ -1,0 +1,102 @@
+"""Parity of the large-vocabulary kernel for rows that keep more than 1024 tokens (top-k 0 = every
+token: the constrained-decoding sweep, configuration 5) with the oracle: token ids exactly equal (a
+mismatch is tolerated only within 1e-12 of a cumulative-share boundary, as in test_gpu_parity), statuses
+exactly equal. The fast path (histogram of the softmax mass, the two crossing buckets sorted) and the
+exact path (every kept token sorted, the reference's sequential sums) are both exercised: the candidate
+export always takes the exact path, and so do rows whose top_p no running share reaches."""
+import numpy as np
+import pytest
+
+import speech_sampler as ss
+import speech_workloads as wl
+from oracle import MASK_ALLOW, MASK_BAN, MASK_NONE, params
+
+from test_gpu_parity import assert_ids, engine_run
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("density", [0.001, 0.01, 0.1, 0.5])
+def test_config5_allow_mask(engine, oracle, density):
+    c = wl.config5(rows=6, density=density)
+    p = params(**c["params"])
+    ids, st = engine_run(engine, c["logits"], ss.params(**c["params"]), mask=c["mask"], mask_kind=MASK_ALLOW, u=c["u"])
+    want, wst, _ = oracle.sample_rows(c["logits"], p, mask=c["mask"], mask_kind=MASK_ALLOW, u=c["u"])
+    near = assert_ids(oracle, ids, st, want, wst, c["logits"], lambda r: p, lambda r: None, lambda r: c["mask"][r],
+                      MASK_ALLOW, c["u"])
+    assert near == 0
+
+
+def test_every_token_no_mask(engine, oracle):
+    rng = np.random.default_rng(51)
+    x = (rng.standard_normal((4, 151936), dtype=np.float32) * np.float32(2.0))
+    u = rng.random(4)
+    for kw in (dict(temperature=1.0, top_k=0, top_p=0.9), dict(temperature=0.7, top_k=0, top_p=0.5),
+               dict(temperature=1.3, top_k=5000, top_p=0.95)):
+        p = params(**kw)
+        ids, st = engine_run(engine, x, ss.params(**kw), u=u)
+        want, wst, _ = oracle.sample_rows(x, p, u=u)
+        assert_ids(oracle, ids, st, want, wst, x, lambda r: p, lambda r: None, lambda r: None, MASK_NONE, u)
+
+
+def test_bf16_history_large_k(engine, oracle):
+    c = wl.config4(rows=4)
+    kw = dict(c["params"], top_k=2000)
+    p = params(**kw)
+    ids, st = engine_run(engine, c["logits_bf16"], ss.params(**kw), c["history"], u=c["u"])
+    want, wst, _ = oracle.sample_rows(c["logits_bf16"], p, history=c["history"], u=c["u"])
+    assert_ids(oracle, ids, st, want, wst, c["logits_bf16"], lambda r: p, lambda r: c["history"][r], lambda r: None,
+               MASK_NONE, c["u"])
+
+
+def test_no_cut_and_single_token(engine, oracle):
+    """top_p 1: every token (the -inf ones too) is kept and pick()'s fallback is the last of them; an
+    allow mask of one token; a ban mask over everything but three tokens."""
+    rng = np.random.default_rng(52)
+    v = 20000
+    x = rng.standard_normal((3, v), dtype=np.float32)
+    allow = np.zeros((3, v), bool)
+    allow[0, rng.choice(v, 300, replace=False)] = True
+    allow[1, 777] = True
+    allow[2, [5, 6000, 19999]] = True
+    m = wl.pack_mask(allow)
+    for kw, u in ((dict(top_k=0, top_p=1.0), np.array([0.3, 0.99, 0.999999])),
+                  (dict(top_k=0, top_p=0.9), np.array([0.0, 0.5, 1.0]))):
+        p = params(**kw)
+        ids, st = engine_run(engine, x, ss.params(**kw), mask=m, mask_kind=MASK_ALLOW, u=u)
+        want, wst, _ = oracle.sample_rows(x, p, mask=m, mask_kind=MASK_ALLOW, u=u)
+        assert_ids(oracle, ids, st, want, wst, x, lambda r: p, lambda r: None, lambda r: m[r], MASK_ALLOW, u)
+
+
+def test_candidates_export_exact_path(engine, oracle):
+    c = wl.config5(rows=3, density=0.01)
+    p = params(**c["params"])
+    cap = 64
+    ids, st, tok, w, cnt, _ = engine_run(engine, c["logits"], ss.params(**c["params"]), mask=c["mask"],
+                                         mask_kind=MASK_ALLOW, u=c["u"], cap=cap)
+    for r in range(3):
+        o = oracle.sample_row(c["logits"][r], p, None, c["mask"][r], MASK_ALLOW, c["u"][r], cap=cap)
+        assert ids[r] == o["id"] and st[r] == o["status"] == ss.ROW_OK
+        assert cnt[r] == o["count"]
+        m = min(cap, o["count"])
+        assert np.array_equal(tok[r, :m], o["tokens"][:m])
+        np.testing.assert_allclose(w[r, :m], o["weights"][:m], rtol=1e-12, atol=0)
+
+
+def test_statuses_and_mixed_rows(engine, oracle):
+    """NaN and all-banned rows, a greedy row and per-row top-k in one launch (max_top_k 0)."""
+    rng = np.random.default_rng(53)
+    v = 30000
+    x = rng.standard_normal((4, v), dtype=np.float32)
+    x[1, 123] = np.nan
+    ban = np.zeros((4, v), bool)
+    ban[2] = True
+    m = wl.pack_mask(ban)
+    rows = [params(top_k=0, top_p=0.9), params(top_k=0, top_p=0.9), params(top_k=0, top_p=0.9), params(greedy=True)]
+    u = rng.random(4)
+    ids, st = engine_run(engine, x, ss.params(top_k=0, top_p=0.9), mask=m, mask_kind=MASK_BAN, u=u,
+                         row_params=[ss.params(greedy=bool(r.greedy), top_k=r.top_k, top_p=r.top_p) for r in rows],
+                         max_top_k=0)
+    want, wst, _ = oracle.sample_rows(x, rows, mask=m, mask_kind=MASK_BAN, u=u)
+    assert list(st) == list(wst)
+    assert list(ids) == list(want)
