@@ -1,6 +1,6 @@
 // The C ABI of include/speech_sampler_b200.h: argument checks, the choice of kernel, the context's
 // scratch, and the host-buffer entry point. No CPU sampling exists behind it: every row is sampled by
-// the CUDA kernels of ssb_small.cu / ssb_stream.cu, or the call fails.
+// the CUDA kernels (ssb_small.cu, ssb_select.cu, ssb_topk.cu, ssb_stream.cu, ssb_nucleus.cu), or the call fails.
 #include <algorithm>
 #include <chrono>
 #include <cstdint>
@@ -71,6 +71,19 @@ ssb_status use_device(const ssb_context * ctx) {
 }
 
 int64_t div_up(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Grows the nucleus kernel's candidate lists to `grid` regions of `ld` composites (never shrinks).
+ssb_status ensure_nucleus_scratch(ssb_context * ctx, int grid, int64_t ld) {
+    const size_t need = (size_t) grid * (size_t) ld * sizeof(uint64_t);
+    if (need <= ctx->nuc_bytes) return SSB_OK;
+    cudaFree(ctx->nuc_scratch);
+    ctx->nuc_scratch = nullptr;
+    ctx->nuc_bytes = 0;
+    const cudaError_t e = cudaMalloc(&ctx->nuc_scratch, need);
+    if (e != cudaSuccess) return cuda_fail(e, "nucleus scratch");
+    ctx->nuc_bytes = need;
+    return SSB_OK;
+}
 
 struct Plan {
     int kernel;  // 0 small, 1 stream (select / top-k / stream kernels), 2 nucleus (top-k above kStreamMaxK)
@@ -187,15 +200,8 @@ ssb_status run(ssb_context * ctx, const ssb_rows * r, const Debug * dbg, cudaStr
         if (occ <= 0) return fail(SSB_DEVICE, "the nucleus kernel does not fit on this device");
         const int grid = std::min(r->rows, ctx->sm_count * occ);
         na.scratch_ld = ssb::nucleus_scratch_ld(r->vocab);
-        const size_t need = (size_t) grid * (size_t) na.scratch_ld * sizeof(uint64_t);
-        if (need > ctx->nuc_bytes) {
-            cudaFree(ctx->nuc_scratch);
-            ctx->nuc_scratch = nullptr;
-            ctx->nuc_bytes = 0;
-            e = cudaMalloc(&ctx->nuc_scratch, need);
-            if (e != cudaSuccess) return cuda_fail(e, "nucleus scratch");
-            ctx->nuc_bytes = need;
-        }
+        const ssb_status gs = ensure_nucleus_scratch(ctx, grid, na.scratch_ld);
+        if (gs != SSB_OK) return gs;
         na.scratch = ctx->nuc_scratch;
         e = ssb::launch_nucleus(na, grid, bf16, debug, stream);
         if (e != cudaSuccess) return cuda_fail(e, "nucleus kernel launch");
@@ -351,7 +357,8 @@ ssb_status ssb_context_reserve(ssb_context * ctx, int32_t max_rows, int32_t max_
     if (!ctx) return fail(SSB_INVALID_ARGUMENT, "ctx is null");
     if (max_rows < 0 || max_vocab < 0) return fail(SSB_INVALID_ARGUMENT, "negative size");
     // Split-row scratch is allocated at creation; reserving sizes the host-call staging buffer for
-    // f32 rows, histories of up to SSB_MAX_STREAM_HISTORY ids and per-row masks.
+    // f32 rows, histories of up to SSB_MAX_STREAM_HISTORY ids and per-row masks, and the candidate
+    // lists of rows that keep more than kStreamMaxK tokens.
     ssb_status s = use_device(ctx);
     if (s != SSB_OK) return s;
     const size_t rows = (size_t) max_rows, vocab = (size_t) max_vocab;
@@ -364,6 +371,15 @@ ssb_status ssb_context_reserve(ssb_context * ctx, int32_t max_rows, int32_t max_
         cudaError_t e = cudaMalloc(&ctx->stage, need);
         if (e != cudaSuccess) return cuda_fail(e, "staging buffer");
         ctx->stage_bytes = need;
+    }
+    // rows that keep more than kStreamMaxK tokens: one list region per resident nucleus CTA (the
+    // occupancy without a history table is the largest the launch can have)
+    if (max_vocab > SSB_SMALL_VOCAB && max_rows > 0) {
+        const size_t smem = ssb::nucleus_smem_bytes(max_vocab, 0);
+        const int occ = std::max(ssb::nucleus_blocks_per_sm(true, smem), ssb::nucleus_blocks_per_sm(false, smem));
+        if (occ <= 0) return fail(SSB_DEVICE, "the nucleus kernel does not fit on this device");
+        s = ensure_nucleus_scratch(ctx, std::min(max_rows, ctx->sm_count * occ), ssb::nucleus_scratch_ld(max_vocab));
+        if (s != SSB_OK) return s;
     }
     return ok();
 }

@@ -100,3 +100,33 @@ def test_statuses_and_mixed_rows(engine, oracle):
     want, wst, _ = oracle.sample_rows(x, rows, mask=m, mask_kind=MASK_BAN, u=u)
     assert list(st) == list(wst)
     assert list(ids) == list(want)
+
+
+def test_reserve_then_graph_capture(oracle):
+    """ssb_context_reserve sizes the nucleus lists, so a top-k 0 launch can be captured into a CUDA graph
+    by a fresh context (capture forbids cudaMalloc) and replayed."""
+    import torch
+    c = wl.config5(rows=8, density=0.01)
+    p = params(**c["params"])
+    s = ss.Sampler(0)
+    try:
+        s.reserve(8, 151936)
+        x = torch.from_numpy(c["logits"]).cuda()
+        m = torch.from_numpy(c["mask"].view(np.int32)).cuda()
+        u = torch.from_numpy(c["u"]).cuda()
+        ids = torch.empty(8, dtype=torch.int32, device="cuda")
+        st = torch.empty(8, dtype=torch.int32, device="cuda")
+        stream = torch.cuda.Stream()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            s.sample(x, ss.params(**c["params"]), mask=m, mask_kind=MASK_ALLOW, u=u, ids=ids, status=st,
+                     stream=torch.cuda.current_stream())
+        ids.fill_(-7)
+        g.replay()
+        torch.cuda.synchronize()
+        want, wst, _ = oracle.sample_rows(c["logits"], p, mask=c["mask"], mask_kind=MASK_ALLOW, u=c["u"])
+        assert list(st.cpu().numpy()) == list(wst)
+        assert list(ids.cpu().numpy()) == list(want)
+        del g
+    finally:
+        s.close()
