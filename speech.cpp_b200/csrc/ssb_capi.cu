@@ -1,6 +1,6 @@
 // The C ABI of include/speech_sampler_b200.h: argument checks, the choice of kernel, the context's
 // scratch, and the host-buffer entry point. No CPU sampling exists behind it: every row is sampled by
-// the CUDA kernels (ssb_small.cu, ssb_select.cu, ssb_topk.cu, ssb_stream.cu, ssb_nucleus.cu), or the call fails.
+// the CUDA kernels (ssb_small.cu, ssb_topk.cu, ssb_stream.cu, ssb_nucleus.cu), or the call fails.
 #include <algorithm>
 #include <chrono>
 #include <cstdint>
@@ -34,9 +34,9 @@ struct ssb_context {
     cudaEvent_t done = nullptr;
     // occupancy of the streaming kernel per (mode, bf16, vec), measured at the row's full width
     int occupancy[2][2][2] = {};
-    // occupancy of the selection kernel per (warp-queue width class, bf16)
-    int occ_select[4][2] = {};
-    size_t occ_select_smem[4][2] = {};  // the shared memory each was measured at
+    // occupancy of the top-k kernel per (warp-list width class, bf16)
+    int occ_topk[3][2] = {};
+    size_t occ_topk_smem[3][2] = {};  // the shared memory each was measured at
 };
 
 namespace {
@@ -86,7 +86,7 @@ ssb_status ensure_nucleus_scratch(ssb_context * ctx, int grid, int64_t ld) {
 }
 
 struct Plan {
-    int kernel;  // 0 small, 1 stream (select / top-k / stream kernels), 2 nucleus (top-k above kStreamMaxK)
+    int kernel;  // 0 small, 1 stream (top-k / stream kernels), 2 nucleus (top-k above kStreamMaxK)
     int mode;    // stream: 0 greedy, 1 top-k
     int k_bound;
 };
@@ -217,30 +217,31 @@ ssb_status run(ssb_context * ctx, const ssb_rows * r, const Debug * dbg, cudaStr
     sa.hist_slots = r->history ? ssb::next_pow2((int) std::max<int64_t>(4, 2 * r->history_ld)) : 0;  // hash, load <= 1/2
     sa.cap = mode == 1 ? (int) div_up(kb + std::max(1024, kb), 32) * 32 : 0;
     sa.sel_slots = mode == 1 ? ssb::next_pow2(std::max(kb, 2)) : 0;
-    // aligned rows with a small top-k (or all greedy) take the warp-specialized selection kernel
-    bool use_select = vec && (mode == 0 || kb <= ssb::kSelectMaxK);
-    const int kw = use_select ? ssb::select_kw(kb, mode == 0) : -1;
+    // aligned rows with a small top-k (or all greedy: top-1) take the warp-specialized top-k kernel
+    bool use_topk = vec && (mode == 0 || kb <= ssb::kTopkMaxK);
+    const int kw = use_topk ? ssb::topk_kw(kb) : -1;
+    const int kwc = kw == 1 ? 0 : (kw == 2 ? 1 : 2);  // its width class
     const int full_chunk = (int) div_up(r->vocab, 32) * 32;
-    // the selection kernels keep per-chunk state in shared memory: cap the chunk so that it fits
+    // the top-k kernel keeps per-chunk state in shared memory: cap the chunk so that it fits
     int max_chunk = full_chunk;
-    if (use_select) {
-        max_chunk = std::min(full_chunk, ssb::select_max_chunk(kw, bf16));
-        while (max_chunk > 4096 && ssb::select_smem_bytes(kw, bf16, max_chunk, sa.hist_slots, sa.sel_slots) > (size_t) ctx->max_smem)
+    if (use_topk) {
+        max_chunk = std::min(full_chunk, ssb::topk_max_chunk(bf16));
+        while (max_chunk > 4096 && ssb::topk_smem_bytes(kw, bf16, max_chunk, sa.hist_slots, sa.sel_slots) > (size_t) ctx->max_smem)
             max_chunk = (int) div_up(max_chunk / 2, 32) * 32;
-        if (ssb::select_smem_bytes(kw, bf16, max_chunk, sa.hist_slots, sa.sel_slots) > (size_t) ctx->max_smem) use_select = false;
+        if (ssb::topk_smem_bytes(kw, bf16, max_chunk, sa.hist_slots, sa.sel_slots) > (size_t) ctx->max_smem) use_topk = false;
     }
-    int occ_select_now = 0;
-    int & occ = use_select ? occ_select_now : ctx->occupancy[mode][bf16][vec];
-    if (use_select) {
+    int occ_topk_now = 0;
+    int & occ = use_topk ? occ_topk_now : ctx->occupancy[mode][bf16][vec];
+    if (use_topk) {
         // per history size, so measured for this call's shared memory (a cached value per width class)
-        int & cached = ctx->occ_select[kw == 0 ? 0 : (kw == 1 ? 1 : (kw == 2 ? 2 : 3))][bf16];
-        const size_t smem = ssb::select_smem_bytes(kw, bf16, max_chunk, sa.hist_slots, sa.sel_slots);
-        if (cached == 0 || ctx->occ_select_smem[kw == 0 ? 0 : (kw == 1 ? 1 : (kw == 2 ? 2 : 3))][bf16] != smem) {
-            cached = ssb::select_blocks_per_sm(kw, bf16, smem);
-            ctx->occ_select_smem[kw == 0 ? 0 : (kw == 1 ? 1 : (kw == 2 ? 2 : 3))][bf16] = smem;
+        int & cached = ctx->occ_topk[kwc][bf16];
+        const size_t smem = ssb::topk_smem_bytes(kw, bf16, max_chunk, sa.hist_slots, sa.sel_slots);
+        if (cached == 0 || ctx->occ_topk_smem[kwc][bf16] != smem) {
+            cached = ssb::topk_blocks_per_sm(kw, bf16, smem);
+            ctx->occ_topk_smem[kwc][bf16] = smem;
         }
         occ = cached;
-        if (occ <= 0) return fail(SSB_DEVICE, "the selection kernel does not fit on this device");
+        if (occ <= 0) return fail(SSB_DEVICE, "the top-k kernel does not fit on this device");
     } else if (occ == 0) {
         occ = ssb::stream_blocks_per_sm(mode, bf16, vec, ssb::stream_smem_bytes(mode, vec, full_chunk, sa.hist_slots, sa.cap, sa.sel_slots));
         if (occ <= 0) return fail(SSB_DEVICE, "the streaming kernel does not fit on this device");
@@ -262,7 +263,7 @@ ssb_status run(ssb_context * ctx, const ssb_rows * r, const Debug * dbg, cudaStr
         sa.counters = ctx->counters;
     }
     if ((int64_t) r->rows * splits > INT32_MAX) return fail(SSB_OUT_OF_RANGE, "too many rows for one launch");
-    e = use_select ? ssb::launch_select(sa, kw, bf16, debug, stream) : ssb::launch_stream(sa, mode, bf16, vec, debug, stream);
+    e = use_topk ? ssb::launch_topk(sa, kw, bf16, debug, stream) : ssb::launch_stream(sa, mode, bf16, vec, debug, stream);
     if (e != cudaSuccess) return cuda_fail(e, "streaming kernel launch");
     return ok();
 }

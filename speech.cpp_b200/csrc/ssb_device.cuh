@@ -520,4 +520,102 @@ __device__ inline void finalize_draw_warp(const uint64_t * sorted, int k, const 
     }
 }
 
+// Margin that separates the crossings of the parallel draw from those of the reference's sequential
+// sums. The reference divides each weight by its sequential total, accumulates the shares in order and
+// (for pick()) renormalizes by the kept total; the parallel draw compares prefix sums of the same
+// exponentials (summed in another order) against top_p times their total, and against u times the kept
+// prefix. With n <= 128 terms >= 0, every one of these sums and quotients lies within 8 n u (u = 2^-53)
+// of its exact value, relative to the total: under 1.2e-13. Crossings farther than kDrawMargin (times
+// the total) from their limits are decided identically.
+constexpr double kDrawMargin = 1e-11;
+
+// The draw of one row by one warp without divisions and with warp scans instead of sequential chains
+// (k <= 128): e_i = exp(s_i - max) as the reference computes them, E_i their running sums (four per
+// lane, then a warp scan), S = E_{k-1}. The top-p cut is the first i with E_i >= top_p S, pick() the
+// first i < keep - 1 with E_i > u E_{keep-1} (else keep - 1). The id equals finalize_draw_warp's
+// whenever each decided comparison clears its limit by kDrawMargin of the total; otherwise it returns
+// false without writing anything and the caller runs finalize_draw_warp. Registers and shuffles only.
+__device__ __forceinline__ bool draw_parallel(const uint64_t * sorted, int k, const RowParams & p, double u,
+                                              const RowOut & out) {
+    const int lane = lane_id();
+    const float max_logit = composite_value(sorted[0]);
+    if (!(max_logit > -kInf && max_logit < kInf)) return false;
+    double e[4];
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+        const int i = 4 * lane + r;
+        e[r] = i < k ? exp((double) composite_value(sorted[i]) - (double) max_logit) : 0.0;
+    }
+    // running sums in index order: lane-local, then a warp scan of the lanes' totals
+    e[1] = __dadd_rn(e[0], e[1]);
+    e[2] = __dadd_rn(e[1], e[2]);
+    e[3] = __dadd_rn(e[2], e[3]);
+    double incl = e[3];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const double t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl = __dadd_rn(incl, t);
+    }
+    const double before = __shfl_up_sync(0xffffffffu, incl, 1);
+    if (lane > 0) {
+#pragma unroll
+        for (int r = 0; r < 4; r++) e[r] = __dadd_rn(before, e[r]);
+    }
+    auto get = [&](int i) {  // E_i for a warp-uniform i
+        const int r = i & 3;
+        const double v = r == 0 ? e[0] : (r == 1 ? e[1] : (r == 2 ? e[2] : e[3]));
+        return __shfl_sync(0xffffffffu, v, i >> 2);
+    };
+    auto first = [&](int n, double limit, bool strict) {  // first i < n with E_i >= limit (> when strict), or n
+        int f = 4;
+#pragma unroll
+        for (int r = 3; r >= 0; r--) {
+            const int i = 4 * lane + r;
+            if (i < n && (strict ? e[r] > limit : e[r] >= limit)) f = r;
+        }
+        const unsigned hit = __ballot_sync(0xffffffffu, f < 4);
+        if (!hit) return n;
+        const int fl = __ffs(hit) - 1;
+        return 4 * fl + __shfl_sync(0xffffffffu, f, fl);
+    };
+    const double S = get(k - 1);
+    const double m = kDrawMargin * S;
+    int keep = k;
+    if (p.top_p < 1.0f) {
+        const double lim = (double) p.top_p * S;
+        const int at = first(k, lim, false);
+        if (at < k) {
+            if (!(get(at) >= lim + m)) return false;
+            if (at > 0 && !(get(at - 1) < lim - m)) return false;
+            keep = at + 1;
+        } else if (!(get(k - 1) < lim - m)) {
+            return false;
+        }
+    }
+    const int n = keep - 1;
+    const double kept = get(n);
+    const double lim2 = u * kept;
+    const int ch = first(n, lim2, true);
+    if (ch < n) {
+        if (!(get(ch) > lim2 + m)) return false;
+        if (ch > 0 && !(get(ch - 1) <= lim2 - m)) return false;
+    } else if (n > 0 && !(get(n - 1) <= lim2 - m)) {
+        return false;
+    }
+    if (lane == 0) {
+        *out.id = (int32_t) composite_index(sorted[ch]);
+        *out.status = SSB_ROW_OK;
+        if (out.count) *out.count = keep;
+    }
+    return true;
+}
+
+// The draw of a row by one warp: the parallel draw where it decides the id, else the sequential one
+// (always for the candidate export, which needs the weights).
+__device__ inline void draw_row(const uint64_t * sorted, int k, const RowParams & p, double u, double * w,
+                                const RowOut & out) {
+    if (k <= 128 && !out.tokens && draw_parallel(sorted, k, p, u, out)) return;
+    finalize_draw_warp(sorted, k, p, u, w, out);
+}
+
 }  // namespace ssb

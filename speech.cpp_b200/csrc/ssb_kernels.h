@@ -65,16 +65,12 @@ size_t stream_smem_bytes(int mode, bool vec, int chunk, int hist_slots, int cap,
 cudaError_t launch_stream(const StreamArgs & a, int mode, bool bf16, bool vec, bool debug, cudaStream_t stream);
 int stream_blocks_per_sm(int mode, bool bf16, bool vec, size_t smem);
 
-// Warp-specialized selection kernel (ssb_select.cu) for 16-byte-aligned rows: kw = 0 for all-greedy
-// batches, else the warp-queue width (1, 2 or 4 registers: top-k up to 32, 64, 128).
-constexpr int kSelectMaxK = 128;
-int select_kw(int k_bound, bool all_greedy);
-// the longest chunk (columns) one CTA of the selection kernels streams
-int select_max_chunk(int kw, bool bf16);
-size_t select_smem_bytes(int kw, bool bf16, int chunk, int hist_slots, int sel_slots);
-int select_blocks_per_sm(int kw, bool bf16, size_t smem);
-cudaError_t launch_select(const StreamArgs & a, int kw, bool bf16, bool debug, cudaStream_t stream);
-// the top-k kernel behind launch_select for kw > 0 (ssb_topk.cu)
+// Top-k kernel (ssb_topk.cu) for 16-byte-aligned rows with top-k <= kTopkMaxK, greedy rows as the
+// top-1 of their unscaled logits: kw = the width of its warp lists in registers (1, 2 or 4: top-k up
+// to 32, 64, 128).
+constexpr int kTopkMaxK = 128;
+int topk_kw(int k_bound);
+// the longest chunk (columns) one CTA streams
 int topk_max_chunk(bool bf16);
 size_t topk_smem_bytes(int kw, bool bf16, int chunk, int hist_slots, int sel_slots);
 int topk_blocks_per_sm(int kw, bool bf16, size_t smem);

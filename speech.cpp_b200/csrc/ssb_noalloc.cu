@@ -8,7 +8,7 @@
 // of an allocation on its decode path. ssb_sample_rows needs an ssb_context, and creating one
 // allocates its split-row scratch with cudaMalloc; this entry point needs no context at all.
 //
-// How: the scratch that the split-row selection kernel uses to combine the CTAs of one row lives in a
+// How: the scratch that the split-row top-k kernel uses to combine the CTAs of one row lives in a
 // fixed-size array in this file, `g_scratch` (kScratchBytes, about 2.03 MiB, held by every GPU that
 // loads the library until the process exits). Host code cannot use the array's name as a device
 // address, so the first call on each device looks the address up with cudaGetSymbolAddress (with that
@@ -16,7 +16,7 @@
 // passes every input and output buffer.
 //
 // Limits: rows of more than SSB_SMALL_VOCAB tokens, 16-byte-aligned rows, and top-k of at most 128
-// (or greedy rows) — the rows the selection kernel (ssb_select.cu) takes; anything else is refused
+// (or greedy rows) — the rows the top-k kernel (ssb_topk.cu) takes; anything else is refused
 // with SSB_OUT_OF_RANGE and a message, never sampled another way. The kernel is launched exactly as
 // ssb_sample_rows launches it; only where its scratch comes from differs.
 //
@@ -42,7 +42,7 @@ void set_last_error(const std::string & message);  // ssb_capi.cu
 namespace {
 
 constexpr int kScratchSlots = 2048;  // (row, split) pairs one launch may spread over
-constexpr int kScratchMaxK = ssb::kSelectMaxK;
+constexpr int kScratchMaxK = ssb::kTopkMaxK;
 constexpr size_t kCandBytes = (size_t) kScratchSlots * kScratchMaxK * sizeof(uint64_t);
 constexpr size_t kScratchBytes = kCandBytes + 4 * (size_t) kScratchSlots * sizeof(uint32_t);
 constexpr int kMaxDevices = 64;
@@ -142,7 +142,7 @@ extern "C" ssb_status ssb_sample_rows_noalloc(const ssb_rows * r, void * stream_
 
     const bool bf16 = r->dtype == SSB_BF16;
     kb = std::max(1, kb);
-    const int kw = ssb::select_kw(kb, all_greedy);
+    const int kw = ssb::topk_kw(kb);
     ssb::StreamArgs sa{};
     ssb::RowsArgs & a = sa.r;
     a.logits = r->logits;
@@ -164,12 +164,12 @@ extern "C" ssb_status ssb_sample_rows_noalloc(const ssb_rows * r, void * stream_
     sa.hist_slots = r->history ? ssb::next_pow2((int) std::max<int64_t>(4, 2 * r->history_ld)) : 0;
     sa.sel_slots = ssb::next_pow2(std::max(kb, 2));
     const int full_chunk = (int) div_up(r->vocab, 32) * 32;
-    const int max_chunk = std::min(full_chunk, ssb::select_max_chunk(kw, bf16));
-    const size_t smem = ssb::select_smem_bytes(kw, bf16, max_chunk, sa.hist_slots, sa.sel_slots);
+    const int max_chunk = std::min(full_chunk, ssb::topk_max_chunk(bf16));
+    const size_t smem = ssb::topk_smem_bytes(kw, bf16, max_chunk, sa.hist_slots, sa.sel_slots);
     if (smem > (size_t) d->max_smem)
-        return fail(SSB_OUT_OF_RANGE, "the history is too long for the selection kernel's shared memory; use ssb_sample_rows");
-    const int occ = ssb::select_blocks_per_sm(kw, bf16, smem);
-    if (occ <= 0) return fail(SSB_DEVICE, "the selection kernel does not fit on this device");
+        return fail(SSB_OUT_OF_RANGE, "the history is too long for the top-k kernel's shared memory; use ssb_sample_rows");
+    const int occ = ssb::topk_blocks_per_sm(kw, bf16, smem);
+    if (occ <= 0) return fail(SSB_DEVICE, "the top-k kernel does not fit on this device");
     const int slots = std::min(kScratchSlots, d->sm_count * occ);
     const int min_chunk = all_greedy ? 2048 : 4096;
     int64_t splits = std::max<int64_t>(1, std::min<int64_t>(div_up(r->vocab, min_chunk), slots / std::max(1, r->rows)));
@@ -190,8 +190,8 @@ extern "C" ssb_status ssb_sample_rows_noalloc(const ssb_rows * r, void * stream_
         e = cudaMemsetAsync(sa.counters, 0, (size_t) r->rows * sizeof(uint32_t), stream);
         if (e != cudaSuccess) return cuda_fail(e, "clearing the arrival counters");
     }
-    e = ssb::launch_select(sa, kw, bf16, false, stream);
-    if (e != cudaSuccess) return cuda_fail(e, "selection kernel launch");
+    e = ssb::launch_topk(sa, kw, bf16, false, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "top-k kernel launch");
     ssb::set_last_error("");
     return SSB_OK;
 }

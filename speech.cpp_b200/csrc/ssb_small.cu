@@ -148,7 +148,7 @@ __global__ void __launch_bounds__(kSmallThreads) small_rows_kernel(const SmallAr
     __syncthreads();
     bitonic_sort_desc(s_cand, kp2);
     const double u = a.u ? a.u[row] : 0.0;
-    if (warp_id() == 0) finalize_draw_warp(s_cand, k, p, u, s_w, out);
+    if (warp_id() == 0) draw_row(s_cand, k, p, u, s_w, out);
 }
 
 template <typename TIn, bool kDebug>

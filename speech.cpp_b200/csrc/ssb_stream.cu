@@ -27,7 +27,7 @@
 // everything below it leaves the buffer. Candidates that find the buffer full stay pending in their
 // thread and are tested again, from the still-resident stage, after the raise. Comparison on
 // composites is exact whatever the order in which elements arrive. At the end the candidates are cut
-// to exactly the k best and sorted, and finalize_draw_warp replays the reference's double-precision
+// to exactly the k best and sorted, and draw_row replays the reference's double-precision
 // softmax, top-p cut and pick.
 #include <climits>
 #include <cuda_bf16.h>
@@ -688,7 +688,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) stream_rows_kernel(const St
         return;
     }
     const double u = a.u ? a.u[row] : 0.0;
-    if (warp_id() == 0) finalize_draw_warp(s_sel, kk, p, u, reinterpret_cast<double *>(s_buf), out);
+    if (warp_id() == 0) draw_row(s_sel, kk, p, u, reinterpret_cast<double *>(s_buf), out);
 }
 
 template <typename TIn, int kMode, bool kVec, bool kDebug>

@@ -1,6 +1,6 @@
-// Pieces shared by the two large-vocabulary stream kernels (ssb_select.cu: greedy; ssb_topk.cu:
-// top-k): TMA bulk copies into a shared-memory ring paced by mbarriers, and the per-lane reductions
-// of the 16-byte groups a consumer lane takes from each stage.
+// Pieces of the large-vocabulary top-k kernel (ssb_topk.cu): TMA bulk copies into a shared-memory ring
+// paced by mbarriers, and the per-lane reductions of the 16-byte groups a consumer lane takes from each
+// stage.
 #pragma once
 
 #include <cstdint>

@@ -16,9 +16,10 @@
 //
 // End phase (short, mostly warp-local).
 //   E1  bound: the lanes' kept maxima are restricted logits of distinct tokens (for fp32 rows the
-//       largest bf16 at or below each). Each consumer warp sorts its lanes' keys and three rounds of
-//       pairwise merges give their exact k-th largest, s_b. k tokens reach s_b, so for a positive temperature
-//       (which keeps the order) every one of the k best has a scaled logit >= c = fl(s_b / T).
+//       largest bf16 at or below each). A two-digit radix select (histograms of the keys' high bytes,
+//       then of the low bytes within the chosen one) gives their exact k-th largest, s_b. k tokens
+//       reach s_b, so for a positive temperature (which keeps the order) every one of the k best has a
+//       scaled logit >= c = fl(s_b / T).
 //   E2  history tokens: penalized (and masked) logits computed now, from the logits the stream has just
 //       brought into L2; candidates if they reach c.
 //   E3  pass 2: every lane keeps its best block's logits in registers through the stream; its other
@@ -31,8 +32,8 @@
 //       blocks could overflow it (or the list), the rounds are synchronized and the array is cut to
 //       its k best by a radix select (which also raises the threshold) between them.
 //   E4  columns past the last whole 16-byte group.
-//   E5  the candidates are ranked (each against all: they are few and distinct), and finalize_draw_warp
-//       replays the reference's double-precision softmax, top-p cut and pick.
+//   E5  the candidates are ranked (each against all: they are few and distinct), and draw_row replays
+//       the reference's double-precision softmax, top-p cut and pick.
 // The restricted maximum (for the row statuses, qwen3-tts/sampler.cpp:43-49) is exact: the largest
 // restricted logit lies in a block whose maximum reaches c, or is a history token.
 // Temperatures that do not keep the order (<= 0 or NaN) make every block a pass-2 block.
@@ -74,60 +75,43 @@ __device__ __forceinline__ int block_word(int gi) {
     return st * kConsumerWarps + (t >> 5);
 }
 
-// Descending bitonic sort of the 32*R u32 of a warp (element r*32 + lane in x[r]).
-template <int R>
-__device__ __forceinline__ void warp_sort_desc_u32(uint32_t (&x)[R]) {
-    const int lane = lane_id();
-#pragma unroll
-    for (int size = 2; size <= 32 * R; size <<= 1) {
-#pragma unroll
-        for (int j = size >> 1; j > 0; j >>= 1) {
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-                const int i = r * 32 + lane;
-                const bool desc = (i & size) == 0;
-                if (j >= 32) {
-                    const int rp = r ^ (j >> 5);
-                    if (rp > r) {
-                        const uint32_t a = x[r], b = x[rp];
-                        if ((a < b) == desc) x[r] = b, x[rp] = a;
-                    }
-                } else {
-                    const uint32_t o = __shfl_xor_sync(0xffffffffu, x[r], j);
-                    const bool keep_max = ((lane & j) == 0) == desc;
-                    x[r] = keep_max ? (x[r] > o ? x[r] : o) : (x[r] < o ? x[r] : o);
-                }
-            }
-        }
-    }
+// Adds one to bin `bin` of a shared histogram for every lane with `take` (plain shared atomics: cheaper
+// here than aggregating equal bins first).
+__device__ __forceinline__ void red_bin(uint32_t * hist, bool take, uint32_t bin) {
+    if (take) atomicAdd(&hist[bin], 1u);
 }
 
-// Merges two descending lists of 32*R u32 (q and t), keeping the best 32*R sorted in q.
-template <int R>
-__device__ __forceinline__ void warp_merge_sorted_u32(uint32_t (&q)[R], const uint32_t (&t)[R]) {
+// In a 256-bin histogram (a larger bin holds larger keys), the bin holding the need-th key from the top,
+// with the number of keys in the bins above it; -1 when the histogram holds fewer than `need` keys.
+// Warp-wide; the result is the same on every lane.
+__device__ __forceinline__ int top_bin(const uint32_t * hist, uint32_t need, uint32_t * above) {
     const int lane = lane_id();
+    // lane L takes bins 255 - 8L down to 248 - 8L
+    const uint4 h0 = reinterpret_cast<const uint4 *>(hist)[63 - 2 * lane];
+    const uint4 h1 = reinterpret_cast<const uint4 *>(hist)[62 - 2 * lane];
+    const uint32_t c[8] = {h0.w, h0.z, h0.y, h0.x, h1.w, h1.z, h1.y, h1.x};
+    uint32_t sum = 0;
 #pragma unroll
-    for (int r = 0; r < R; r++) {
-        const uint32_t o = __shfl_sync(0xffffffffu, t[R - 1 - r], 31 - lane);
-        q[r] = q[r] > o ? q[r] : o;
+    for (int i = 0; i < 8; i++) sum += c[i];
+    uint32_t incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
     }
+    const unsigned hit = __ballot_sync(0xffffffffu, incl >= need);
+    if (!hit) return -1;
+    const int fl = __ffs(hit) - 1;
+    uint32_t run = incl - sum;  // keys in the bins above this lane's
+    int bin = -1;
+    uint32_t ab = 0;
 #pragma unroll
-    for (int j = 16 * R; j > 0; j >>= 1) {
-#pragma unroll
-        for (int r = 0; r < R; r++) {
-            if (j >= 32) {
-                const int rp = r ^ (j >> 5);
-                if (rp > r) {
-                    const uint32_t a = q[r], b = q[rp];
-                    if (a < b) q[r] = b, q[rp] = a;
-                }
-            } else {
-                const uint32_t o = __shfl_xor_sync(0xffffffffu, q[r], j);
-                const bool keep_max = (lane & j) == 0;
-                q[r] = keep_max ? (q[r] > o ? q[r] : o) : (q[r] < o ? q[r] : o);
-            }
-        }
+    for (int i = 0; i < 8; i++) {
+        if (bin < 0 && run + c[i] >= need) bin = 255 - 8 * lane - i, ab = run;
+        run += c[i];
     }
+    *above = __shfl_sync(0xffffffffu, ab, fl);
+    return __shfl_sync(0xffffffffu, bin, fl);
 }
 
 // Slot of history token t in the table, or -1.
@@ -157,7 +141,8 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
     __shared__ float s_redf[32];
     __shared__ int s_redi[32];
     __shared__ int s_count, s_gather, s_abort, s_last, s_n0, s_qn;
-    __shared__ uint32_t s_bound;
+    __shared__ __align__(16) uint32_t s_f1[256];  // bound: histogram of the kept keys' high bytes
+    __shared__ __align__(16) uint32_t s_f2[256];  // and of their low bytes within the chosen high byte
     __shared__ int s_qlist[kListMax];
 
     const int tid = (int) threadIdx.x;
@@ -212,6 +197,7 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
     const bool special = mrow != nullptr || penal;
     const int hbits_n = sa.hist_slots > 1 ? 31 - __clz(sa.hist_slots) : 1;
 
+    for (int i = tid; i < 256; i += blockDim.x) s_f1[i] = 0, s_f2[i] = 0;
     if (tid == 0) {
         s_count = 0;
         s_qn = 0;
@@ -381,37 +367,23 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
     __syncwarp();
 
     // ---- end phase (all threads)
-    // E1: the exact k-th largest of the lanes' kept keys: each consumer warp sorts its 64, then three
-    // rounds of pairwise merges keep the best 32*KW (ring memory: every warp is past pass 1 after the
-    // first barrier)
-    uint32_t * s_lists = reinterpret_cast<uint32_t *>(smem);  // [kConsumerWarps][32 * QN]
+    // E1: the exact k-th largest of the lanes' kept keys, by a two-digit radix select (a histogram of the
+    // high bytes, then of the low bytes within the chosen one; every warp reads each after its barrier,
+    // the second of which also frees the ring's memory for the candidates)
+    red_bin(s_f1, consumer && key0 != 0, key0 >> 8);
+    red_bin(s_f1, consumer && key1 != 0, key1 >> 8);
     __syncthreads();
-    if (consumer) {
-        uint32_t x[2] = {key0, key1};
-        warp_sort_desc_u32<2>(x);
-#pragma unroll
-        for (int r = 0; r < QN; r++) s_lists[warp * 32 * QN + r * 32 + lane] = r < 2 ? x[r < 2 ? r : 0] : 0u;
-    }
+    uint32_t above1 = 0;
+    const int b1 = top_bin(s_f1, (uint32_t) k, &above1);
+    red_bin(s_f2, consumer && b1 >= 0 && key0 != 0 && (int) (key0 >> 8) == b1, key0 & 255u);
+    red_bin(s_f2, consumer && b1 >= 0 && key1 != 0 && (int) (key1 >> 8) == b1, key1 & 255u);
     __syncthreads();
-#pragma unroll 1
-    for (int step = 1; step < kConsumerWarps; step <<= 1) {
-        if (consumer && (warp & (2 * step - 1)) == 0) {
-            uint32_t q[QN], t[QN];
-#pragma unroll
-            for (int r = 0; r < QN; r++) {
-                q[r] = s_lists[warp * 32 * QN + r * 32 + lane];
-                t[r] = s_lists[(warp + step) * 32 * QN + r * 32 + lane];
-            }
-            warp_merge_sorted_u32<QN>(q, t);
-            __syncwarp();
-#pragma unroll
-            for (int r = 0; r < QN; r++) s_lists[warp * 32 * QN + r * 32 + lane] = q[r];
-        }
-        __syncthreads();
+    uint32_t P = 0;
+    if (b1 >= 0) {
+        uint32_t above2 = 0;
+        const int b2 = top_bin(s_f2, (uint32_t) k - above1, &above2);
+        if (b2 >= 0) P = ((uint32_t) b1 << 8) | (uint32_t) b2;
     }
-    if (tid == 0) s_bound = s_lists[k - 1];
-    __syncthreads();  // s_lists is ring memory, about to hold candidates
-    const uint32_t P = s_bound;
     // P <= key of -inf (no k keys): no bound; else the value of key P << 16 is at or below k restricted
     // logits
     const float s_b = (P << 16) <= order_key(-kInf) ? -kInf : key_value(P << 16);
@@ -754,7 +726,7 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
         return;
     }
     const double u = a.u ? a.u[row] : 0.0;
-    if (warp == 0) finalize_draw_warp(s_sel, kk, p, u, reinterpret_cast<double *>(s_cand), out);  // candidate memory as scratch
+    if (warp == 0) draw_row(s_sel, kk, p, u, reinterpret_cast<double *>(s_cand), out);  // candidate memory as scratch
 }
 
 template <typename TIn, int KW, bool kDebug>
@@ -775,6 +747,8 @@ void * pick_kernel(int kw, bool bf16, bool debug) {
 }
 
 }  // namespace
+
+int topk_kw(int k_bound) { return k_bound <= 32 ? 1 : (k_bound <= 64 ? 2 : 4); }
 
 int topk_max_chunk(bool bf16) { return kMaxStages * kStageBytes / (bf16 ? 2 : 4); }
 

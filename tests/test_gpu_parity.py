@@ -325,3 +325,28 @@ def test_repeat_launches_and_host_entry(engine, oracle):
     ids_h, st_h = engine.sample_host(c["logits_bf16"], ss.params(**kw), c["history"], None, None, MASK_NONE, c["u"])
     assert np.array_equal(ids_h, first) and np.all(st_h == 0)
     torch.cuda.synchronize()
+
+
+def test_draw_at_exact_boundaries(engine, oracle):
+    """u placed exactly on pick()'s running sums (added as the reference adds them, in order): the
+    parallel draw cannot decide such rows within its margin and defers to the sequential replay."""
+    c = wl.config4(rows=8)
+    kw = c["params"]
+    p = params(**kw)
+    us = []
+    for r in range(8):
+        o = oracle.sample_row(c["logits_bf16"][r], p, c["history"][r], None, MASK_NONE, 0.5, cap=128)
+        w = [float(x) for x in o["weights"][:o["count"]]]
+        total = 0.0
+        for x in w:
+            total += x
+        cum, cums = 0.0, []
+        for x in w[:-1]:
+            cum += x / total
+            cums.append(cum)
+        us.append(cums[r % len(cums)] if cums else 0.5)
+    u = np.array(us)
+    ids, st = engine_run(engine, c["logits_bf16"], ss.params(**kw), c["history"], u=u)
+    want, wst, _ = oracle.sample_rows(c["logits_bf16"], p, history=c["history"], u=u)
+    assert_ids(oracle, ids, st, want, wst, c["logits_bf16"], lambda r: p, lambda r: c["history"][r], lambda r: None,
+               MASK_NONE, u)
