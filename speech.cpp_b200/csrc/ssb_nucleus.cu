@@ -157,48 +157,105 @@ __global__ void __launch_bounds__(kNThreads, 1) nucleus_rows_kernel(const Nucleu
             }
         }
         __syncthreads();
+        // penalized logit of history column col (raw logit v)
+        auto penalized = [&](int col, float v) {
+            const uint32_t hmask = (uint32_t) na.hist_slots - 1u;
+            uint32_t h = hash_token(col, hbits_n);
+            for (uint32_t n = 0; n <= hmask && s_hkey[h] != col; n++) h = (h + 1) & hmask;
+            return penalize(v, s_hcnt[h], p);
+        };
         // restricted logit of column col
         auto restricted = [&](int col) {
             float v = Elem<TIn>::load1(src, col);
-            if (penal && ((s_hbits[col >> 5] >> (col & 31)) & 1u)) {
-                const uint32_t hmask = (uint32_t) na.hist_slots - 1u;
-                uint32_t h = hash_token(col, hbits_n);
-                for (uint32_t n = 0; n <= hmask && s_hkey[h] != col; n++) h = (h + 1) & hmask;
-                v = penalize(v, s_hcnt[h], p);
-            }
+            if (penal && ((s_hbits[col >> 5] >> (col & 31)) & 1u)) v = penalized(col, v);
             if (mrow && masked_bit(__ldg(mrow + (col >> 5)) >> (col & 31), a.mask_kind)) v = -kInf;
             return v;
         };
 
-        // ---- pass 1: the row; the finite scaled logits go to the list as composites, counted per bucket
+        // ---- pass 1: the row, one mask word (32 columns) per thread and round; the finite scaled logits go
+        // to the list as composites, counted per bucket. A chunk of 8 columns that the mask bans whole is
+        // -inf without being read (the debug export reads every column, for the restricted logits).
         for (int i = tid; i < kBuckets; i += kNThreads) s_hcount[i] = 0;
         __syncthreads();
         float acc = -kInf;
         int nan_scaled = 0;
         uint64_t best = 0;
-        for (int base = 0; base < vocab; base += kNThreads) {  // uniform trip count
-            const int col = base + tid;
-            bool has = false;
-            uint64_t cv = 0;
-            if (col < vocab) {
-                const float v = restricted(col);
-                if (kDebug && a.dbg_processed) a.dbg_processed[(int64_t) row * vocab + col] = v;
-                acc = max_nan(acc, v);
-                const float sc = greedy_row ? v : __fdiv_rn(v, T);
-                nan_scaled |= sc != sc;
-                if (sc == sc && sc > -kInf) {
-                    cv = composite(sc, (uint32_t) col);
-                    has = true;
-                    best = cv > best ? cv : best;
-                    atomicAdd(&s_hcount[bucket_of(cv)], 1);
+        const bool vec = (reinterpret_cast<uintptr_t>(src) & 15u) == 0;  // 16-byte loads of whole chunks
+        const int nwords = (vocab + 31) >> 5;
+        for (int wbase = 0; wbase < nwords; wbase += kNThreads) {  // uniform trip count
+            const int w = wbase + tid;
+            const int col0 = w << 5;
+            uint32_t live = 0, allowed = 0, hbw = 0;
+            if (w < nwords) {
+                live = vocab - col0 >= 32 ? 0xFFFFFFFFu : ((1u << (vocab - col0)) - 1u);
+                allowed = live;
+                if (mrow) {
+                    const uint32_t mw = __ldg(mrow + w);
+                    allowed &= a.mask_kind == SSB_MASK_BAN ? ~mw : mw;
                 }
+                if (penal) hbw = s_hbits[w];
             }
-            const unsigned m = __ballot_sync(0xffffffffu, has);
-            if (m) {
-                int at = 0;
-                if (lane == __ffs(m) - 1) at = atomicAdd(&s_n, __popc(m));
-                at = __shfl_sync(0xffffffffu, at, __ffs(m) - 1);
-                if (has) list[at + __popc(m & ((1u << lane) - 1u))] = cv;
+            const uint32_t visit = kDebug ? live : allowed;
+            // the chunks' logits, read together (16-byte loads where the chunk is whole and aligned)
+            constexpr int kPerChunk = 8 * (int) sizeof(TIn) / 16;  // 16-byte loads per 8 columns
+            uint4 raw[4 * kPerChunk];
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const bool load = ((visit >> (8 * c)) & 0xFFu) != 0 && vec && ((live >> (8 * c)) & 0xFFu) == 0xFFu;
+#pragma unroll
+                for (int q = 0; q < kPerChunk; q++)
+                    raw[c * kPerChunk + q] = load ? ld_stream(src + col0 + 8 * c + q * (16 / (int) sizeof(TIn))) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const uint32_t vis = (visit >> (8 * c)) & 0xFFu;
+                const bool whole = vec && ((live >> (8 * c)) & 0xFFu) == 0xFFu;
+                uint64_t cv[8];
+                uint32_t has = 0;
+                if (vis) {
+                    float x[8];
+                    if (whole) {
+#pragma unroll
+                        for (int q = 0; q < kPerChunk; q++) Elem<TIn>::unpack(raw[c * kPerChunk + q], x + q * (8 / kPerChunk));
+                    }
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        const int bit = 8 * c + e, col = col0 + bit;
+                        if ((vis >> e) & 1u) {
+                            float v = whole ? x[e] : Elem<TIn>::load1(src, col);
+                            if (!((allowed >> bit) & 1u)) v = -kInf;
+                            else if ((hbw >> bit) & 1u) v = penalized(col, v);
+                            if (kDebug && a.dbg_processed) a.dbg_processed[(int64_t) row * vocab + col] = v;
+                            acc = max_nan(acc, v);
+                            if ((allowed >> bit) & 1u) {
+                                const float sc = greedy_row ? v : __fdiv_rn(v, T);
+                                nan_scaled |= sc != sc;
+                                if (sc == sc && sc > -kInf) {
+                                    cv[e] = composite(sc, (uint32_t) col);
+                                    has |= 1u << e;
+                                    best = cv[e] > best ? cv[e] : best;
+                                    atomicAdd(&s_hcount[bucket_of(cv[e])], 1);
+                                }
+                            }
+                        }
+                    }
+                }
+                if (__any_sync(0xffffffffu, has != 0)) {
+                    // one shared atomic per warp: a scan of the lanes' counts gives each its place
+                    const int n = __popc(has);
+                    int incl = n;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+                        if (lane >= o) incl += t;
+                    }
+                    int at = 0;
+                    if (lane == 31) at = atomicAdd(&s_n, incl);
+                    at = __shfl_sync(0xffffffffu, at, 31) + incl - n;
+#pragma unroll
+                    for (int e = 0; e < 8; e++)
+                        if ((has >> e) & 1u) list[at + __popc(has & ((1u << e) - 1u))] = cv[e];
+                }
             }
         }
         const float row_max = block_max_nan(acc, s_redf);
