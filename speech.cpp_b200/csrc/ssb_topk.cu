@@ -197,6 +197,13 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
     const bool special = mrow != nullptr || penal;
     const int hbits_n = sa.hist_slots > 1 ? 31 - __clz(sa.hist_slots) : 1;
 
+    // each thread's first history ids, requested before the first stages' copies
+    int32_t hpre[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        const int i = q * kTkThreads + tid;
+        hpre[q] = penal && i < hlen ? __ldg(hist + i) : -1;
+    }
     for (int i = tid; i < 256; i += blockDim.x) s_f1[i] = 0, s_f2[i] = 0;
     if (tid == 0) {
         s_count = 0;
@@ -229,7 +236,7 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
 #pragma unroll
                 for (int q = 0; q < 4; q++) {  // four independent loads in flight
                     const int i = base + q * kTkThreads + tid;
-                    t[q] = i < hlen ? __ldg(hist + i) : -1;
+                    t[q] = base == 0 ? hpre[q] : (i < hlen ? __ldg(hist + i) : -1);
                 }
                 bool first[4];
 #pragma unroll
@@ -259,7 +266,7 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
 #pragma unroll
                 for (int q = 0; q < 4; q++) {
                     const int i = base + q * kTkThreads + tid;
-                    const int32_t t = i < hlen ? __ldg(hist + i) : -1;
+                    const int32_t t = base == 0 ? hpre[q] : (i < hlen ? __ldg(hist + i) : -1);
                     if (t >= c0 && t < c1) atomicAdd(&s_hcnt[hist_slot(s_hkey, hbits_n, t)], 1);
                 }
             }
