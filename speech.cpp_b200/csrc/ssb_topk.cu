@@ -4,8 +4,8 @@
 // One CTA streams `chunk` consecutive columns of one row (several CTAs per row when the batch is small;
 // the last to finish merges their lists, as in ssb_stream.cu). Two passes:
 //
-// Before the stream: the row's history table (distinct ids with their counts) and a bitmap of the
-// blocks holding a history or a masked token ("special" blocks; every other block's raw logits are its
+// Before the stream: the row's history table (distinct ids with their counts, built in one pass of
+// insert-or-find and count) and a bitmap of the blocks holding a history or a masked token ("special" blocks; every other block's raw logits are its
 // restricted logits, qwen3-tts/sampler.cpp:29-51), built by all threads while the first stages load.
 //
 // Pass 1, the stream. A producer warp brings the chunk through a ring of kTkStages 16 KB shared-memory
@@ -228,8 +228,8 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
         }
         __syncthreads();
         if (penal) {
-            // the first occurrence of an id (its column bit was clear) inserts it into the table; then
-            // every occurrence counts itself
+            // one pass: every occurrence of an id finds or takes its slot and counts itself there; the
+            // column bit and the block bit are set by every occurrence alike
             const uint32_t hmask = (uint32_t) sa.hist_slots - 1u;
             for (int base = 0; base < hlen; base += 4 * kTkThreads) {  // uniform trip count
                 int32_t t[4];
@@ -238,36 +238,23 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
                     const int i = base + q * kTkThreads + tid;
                     t[q] = base == 0 ? hpre[q] : (i < hlen ? __ldg(hist + i) : -1);
                 }
-                bool first[4];
 #pragma unroll
                 for (int q = 0; q < 4; q++) {
-                    first[q] = false;
                     if (t[q] >= c0 && t[q] < c1) {
                         const int rel = t[q] - c0;
-                        const uint32_t bit = 1u << (rel & 31);
-                        first[q] = !(atomicOr(&s_hbits[rel >> 5], bit) & bit);
-                    }
-                }
-#pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    if (first[q]) {
+                        atomicOr(&s_hbits[rel >> 5], 1u << (rel & 31));
+                        const int gi = rel / G;
+                        if (gi < nvec) atomicOr(&s_bb[block_word(gi)], 1u << (gi & 31));
                         uint32_t h = hash_token(t[q], hbits_n);
-                        for (uint32_t n = 0; n <= hmask; n++) {  // distinct keys: only empty slots are taken
-                            if (atomicCAS(&s_hkey[h], -1, t[q]) == -1) break;
+                        for (uint32_t n = 0; n <= hmask; n++) {
+                            const int32_t old = atomicCAS(&s_hkey[h], -1, t[q]);
+                            if (old == -1 || old == t[q]) {
+                                atomicAdd(&s_hcnt[h], 1);
+                                break;
+                            }
                             h = (h + 1) & hmask;
                         }
-                        const int gi = (t[q] - c0) / G;
-                        if (gi < nvec) atomicOr(&s_bb[block_word(gi)], 1u << (gi & 31));
                     }
-                }
-            }
-            __syncthreads();
-            for (int base = 0; base < hlen; base += 4 * kTkThreads) {
-#pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    const int i = base + q * kTkThreads + tid;
-                    const int32_t t = base == 0 ? hpre[q] : (i < hlen ? __ldg(hist + i) : -1);
-                    if (t >= c0 && t < c1) atomicAdd(&s_hcnt[hist_slot(s_hkey, hbits_n, t)], 1);
                 }
             }
         }
