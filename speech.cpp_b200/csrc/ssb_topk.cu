@@ -5,8 +5,9 @@
 // the last to finish merges their lists, as in ssb_stream.cu). Two passes:
 //
 // Before the stream: the row's history table (distinct ids with their counts, built in one pass of
-// insert-or-find and count) and a bitmap of the blocks holding a history or a masked token ("special" blocks; every other block's raw logits are its
-// restricted logits, qwen3-tts/sampler.cpp:29-51), built by all threads while the first stages load.
+// insert-or-find and count) and a bitmap of the blocks holding a history or a masked token ("special"
+// blocks; every other block's raw logits are its restricted logits, qwen3-tts/sampler.cpp:29-51),
+// built by all threads while the first stages load.
 //
 // Pass 1, the stream. A producer warp brings the chunk through a ring of kTkStages 16 KB shared-memory
 // stages with TMA bulk copies (cp.async.bulk + mbarrier complete_tx) and refills a slot as soon as every
