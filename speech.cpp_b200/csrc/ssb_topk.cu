@@ -29,6 +29,8 @@
 //       is not a history token is restricted (-inf where masked), divided by the temperature exactly as
 //       the reference does (qwen3-tts/sampler.cpp:73) and keyed as a composite (value, then lowest
 //       index: the order of qwen3-tts/sampler.cpp:78-79 with haru/sampler.cpp:39's tie-break).
+//       A special best block is taken only if its maximum outside the history (masked tokens at -inf)
+//       can reach c, computed from its registers: a history token's raw logit alone does not qualify it.
 //       Composites >= the threshold go to a candidate array in the ring's memory. When the qualifying
 //       blocks could overflow it (or the list), the rounds are synchronized and the array is cut to
 //       its k best by a radix select (which also raises the threshold) between them.
@@ -74,6 +76,20 @@ __device__ __forceinline__ int block_word(int gi) {
     const int st = gi / kStageGroups;
     const int t = gi % kConsumers;
     return st * kConsumerWarps + (t >> 5);
+}
+
+// A group with the elements of bit mask ex (element order) set to -inf.
+template <typename TIn> __device__ __forceinline__ uint4 exclude_group(const uint4 & g, uint32_t ex);
+template <> __device__ __forceinline__ uint4 exclude_group<uint16_t>(const uint4 & g, uint32_t ex) {
+    auto f = [](uint32_t w, uint32_t b) {
+        const uint32_t sel = ((b & 1u) ? 0x0000FFFFu : 0u) | ((b & 2u) ? 0xFFFF0000u : 0u);
+        return (w & ~sel) | (0xFF80FF80u & sel);
+    };
+    return make_uint4(f(g.x, ex), f(g.y, ex >> 2), f(g.z, ex >> 4), f(g.w, ex >> 6));
+}
+template <> __device__ __forceinline__ uint4 exclude_group<float>(const uint4 & g, uint32_t ex) {
+    return make_uint4((ex & 1u) ? 0xFF800000u : g.x, (ex & 2u) ? 0xFF800000u : g.y, (ex & 4u) ? 0xFF800000u : g.z,
+                      (ex & 8u) ? 0xFF800000u : g.w);
 }
 
 // Adds one to bin `bin` of a shared histogram for every lane with `take` (plain shared atomics: cheaper
@@ -511,9 +527,29 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
     // its registers: it is staged in shared memory; its other qualifying blocks (only when its second
     // best can qualify) are read again from L2. All of them are listed and taken cooperatively, one
     // 16-byte group per lane, eight blocks per warp and round.
-    const bool best_q = consumer && best_st >= 0 && qualifies(best_v);
+    const bool lane_q = consumer && best_st >= 0 && qualifies(best_v);  // the lane has a qualifying block
+    bool best_q = lane_q;  // its best block is taken
+    if (best_q && special && ((s_bb[best_st * kConsumerWarps + warp] >> lane) & 1u)) {
+        // a special best block (still in registers) is taken only if its maximum over the tokens outside
+        // the history (masked ones at -inf) can reach the threshold: its history tokens are E2's
+        float lx = -kInf;
+#pragma unroll
+        for (int j = 0; j < kGroupsPerThread; j++) {
+            const int g = j * kConsumers + tid;
+            if (g < min(kStageGroups, nvec - best_st * kStageGroups)) {
+                const int col0 = c0 + best_st * kStageElems + g * G, rel0 = col0 - c0;
+                uint32_t ex = penal ? (s_hbits[rel0 >> 5] >> (rel0 & 31)) & ((1u << G) - 1u) : 0u;
+                if (mrow) {
+                    const uint32_t mw = (__ldg(mrow + (col0 >> 5)) >> (col0 & 31)) & ((1u << G) - 1u);
+                    ex |= a.mask_kind == SSB_MASK_BAN ? mw : (~mw & ((1u << G) - 1u));
+                }
+                lx = max_nan(lx, group_max<TIn>(exclude_group<TIn>(best_rv[j], ex)));
+            }
+        }
+        best_q = qualifies(lx);
+    }
     uint64_t qmask = 0;  // stages of this lane's other qualifying blocks
-    if (best_q && qualifies(second_v))
+    if (lane_q && qualifies(second_v))
         for (int st = 0; st < nstages; st++)
             if (st != best_st && qualifies(__uint_as_float((uint32_t) s_up[st * kConsumers + tid] << 16))) qmask |= 1ull << st;
     const int nq = __popcll(qmask);
