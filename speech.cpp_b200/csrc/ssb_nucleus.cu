@@ -181,18 +181,22 @@ __global__ void __launch_bounds__(kNThreads, 1) nucleus_rows_kernel(const Nucleu
         int nan_scaled = 0;
         uint64_t best = 0;
         const bool vec = (reinterpret_cast<uintptr_t>(src) & 15u) == 0;  // 16-byte loads of whole chunks
+        // a temperature that is a power of two scales exactly by its reciprocal: fl(x * 2^-e) is the
+        // correctly rounded x / 2^e, the same number __fdiv_rn gives
+        const bool pow2 = T > 0.0f && T < kInf && (__float_as_uint(T) & 0x007FFFFFu) == 0u;
+        const float inv_t = pow2 ? __fdiv_rn(1.0f, T) : 0.0f;
         const int nwords = (vocab + 31) >> 5;
+        uint32_t next_mw = mrow && tid < nwords ? __ldg(mrow + tid) : 0u;  // the next round's mask word, read ahead
         for (int wbase = 0; wbase < nwords; wbase += kNThreads) {  // uniform trip count
             const int w = wbase + tid;
             const int col0 = w << 5;
+            const uint32_t mw = next_mw;
+            if (mrow && w + kNThreads < nwords) next_mw = __ldg(mrow + w + kNThreads);
             uint32_t live = 0, allowed = 0, hbw = 0;
             if (w < nwords) {
                 live = vocab - col0 >= 32 ? 0xFFFFFFFFu : ((1u << (vocab - col0)) - 1u);
                 allowed = live;
-                if (mrow) {
-                    const uint32_t mw = __ldg(mrow + w);
-                    allowed &= a.mask_kind == SSB_MASK_BAN ? ~mw : mw;
-                }
+                if (mrow) allowed &= a.mask_kind == SSB_MASK_BAN ? ~mw : mw;
                 if (penal) hbw = s_hbits[w];
             }
             const uint32_t visit = kDebug ? live : allowed;
@@ -228,7 +232,7 @@ __global__ void __launch_bounds__(kNThreads, 1) nucleus_rows_kernel(const Nucleu
                             if (kDebug && a.dbg_processed) a.dbg_processed[(int64_t) row * vocab + col] = v;
                             acc = max_nan(acc, v);
                             if ((allowed >> bit) & 1u) {
-                                const float sc = greedy_row ? v : __fdiv_rn(v, T);
+                                const float sc = greedy_row ? v : (pow2 ? __fmul_rn(v, inv_t) : __fdiv_rn(v, T));
                                 nan_scaled |= sc != sc;
                                 if (sc == sc && sc > -kInf) {
                                     cv[e] = composite(sc, (uint32_t) col);
