@@ -74,3 +74,87 @@ def test_config4_shard_sizes(world):
     assert w["rows"] == 16 // world
     first = wl.config4(rows=1, row0=(world - 1) * (16 // world))
     np.testing.assert_array_equal(w["logits"][0], first["logits_bf16"][0])
+
+
+class _OracleSampler:
+    """The engine's two calls the vocabulary-sharded protocol makes, answered by the CPU oracle on CPU
+    tensors (the protocol's host logic and its exchange are what this tests, on gloo ranks)."""
+
+    def __init__(self, kw):
+        import sys
+        sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle"))
+        from oracle import Oracle, params
+        self.o = Oracle()
+        self.p = params(**kw)
+
+    def candidates(self, logits, p, history, history_len, mask, mask_kind, u, cap=0, processed=True):
+        import torch
+        h = None if history is None else history.numpy()[0]
+        m = None if mask is None else mask.numpy().view(np.uint32)[0]
+        r = self.o.sample_row(logits.numpy()[0], self.p, h, m, mask_kind, float(u[0]), want_processed=True)
+        return None, None, None, None, None, torch.from_numpy(r["processed"].copy()).view(1, -1)
+
+    def sample(self, row, p, history, history_len, mask, mask_kind, u):
+        import torch
+        r = self.o.sample_row(row.numpy()[0], self.p, None, None, 0, float(u[0]))
+        return torch.tensor([r["id"]], dtype=torch.int32), torch.tensor([r["status"]], dtype=torch.int32)
+
+
+def _shard_rank_main(rank, world, port, out):
+    import torch
+    import torch.distributed as dist
+    import speech_vocab_shard as vs
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        c = wl.config4(rows=2)
+        kw = dict(c["params"], repetition_penalty=1.2)
+        sampler = _OracleSampler(kw)
+        rng = np.random.default_rng(7)
+        ban = rng.random((1, c["logits_bf16"].shape[1])) < 0.3
+        mask = torch.from_numpy(wl.pack_mask(ban).view(np.int32))
+        got = []
+        for r in range(2):
+            row = torch.from_numpy(c["logits_bf16"][r:r + 1])
+            off, width = vs.shard_bounds(row.shape[1], world)[rank]
+            ids, st = vs.sample_vocab_sharded(sampler, row[:, off:off + width].contiguous(), row.shape[1], None,
+                                              torch.from_numpy(c["history"][r:r + 1]), mask, 1,
+                                              torch.from_numpy(c["u"][r:r + 1]))
+            got.append((int(ids[0]), int(st[0])))
+        want = [(sampler.o.sample_row(c["logits_bf16"][r], sampler.p, c["history"][r], wl.pack_mask(ban)[0], 1,
+                                      float(c["u"][r]))["id"], 0) for r in range(2)]
+        out.put((rank, got, want))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_vocab_sharded_exchange_two_gloo_ranks():
+    """Each rank restricts its slice (history ids translated, its mask words), the slices are
+    all-gathered, every rank draws from the whole row: both ranks give the whole-row oracle's ids."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_shard_rank_main, args=(r, world, port, out)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        results = [out.get(timeout=180) for _ in range(world)]
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+    for p in procs:
+        assert p.exitcode == 0
+    for rank, got, want in results:
+        assert got == want, (rank, got, want)
+
+
+def test_shard_bounds():
+    import speech_vocab_shard as vs
+    for vocab in (151936, 151937, 3072, 70000):
+        for world in (1, 2, 3, 4, 8):
+            b = vs.shard_bounds(vocab, world)
+            assert b[0][0] == 0 and sum(w for _, w in b) == vocab
+            assert all(off % 32 == 0 for off, _ in b)
+            assert all(b[i][0] + b[i][1] == b[i + 1][0] for i in range(world - 1))
