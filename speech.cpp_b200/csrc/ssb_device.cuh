@@ -237,6 +237,46 @@ __device__ __forceinline__ int block_max_int(int v, int * scratch) {
     return t;
 }
 
+// ---------------------------------------------------------------- 16-bit key histograms
+// Adds one to bin `bin` of a shared histogram for every lane with `take` (plain shared atomics: cheaper
+// here than aggregating equal bins first).
+__device__ __forceinline__ void red_bin(uint32_t * hist, bool take, uint32_t bin) {
+    if (take) atomicAdd(&hist[bin], 1u);
+}
+
+// In a 256-bin histogram (a larger bin holds larger keys), the bin holding the need-th key from the top,
+// with the number of keys in the bins above it; -1 when the histogram holds fewer than `need` keys.
+// Warp-wide; the result is the same on every lane.
+__device__ __forceinline__ int top_bin(const uint32_t * hist, uint32_t need, uint32_t * above) {
+    const int lane = lane_id();
+    // lane L takes bins 255 - 8L down to 248 - 8L
+    const uint4 h0 = reinterpret_cast<const uint4 *>(hist)[63 - 2 * lane];
+    const uint4 h1 = reinterpret_cast<const uint4 *>(hist)[62 - 2 * lane];
+    const uint32_t c[8] = {h0.w, h0.z, h0.y, h0.x, h1.w, h1.z, h1.y, h1.x};
+    uint32_t sum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) sum += c[i];
+    uint32_t incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+    }
+    const unsigned hit = __ballot_sync(0xffffffffu, incl >= need);
+    if (!hit) return -1;
+    const int fl = __ffs(hit) - 1;
+    uint32_t run = incl - sum;  // keys in the bins above this lane's
+    int bin = -1;
+    uint32_t ab = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        if (bin < 0 && run + c[i] >= need) bin = 255 - 8 * lane - i, ab = run;
+        run += c[i];
+    }
+    *above = __shfl_sync(0xffffffffu, ab, fl);
+    return __shfl_sync(0xffffffffu, bin, fl);
+}
+
 // ---------------------------------------------------------------- radix select on composites
 // Shared state of one selection.
 struct SelectState {

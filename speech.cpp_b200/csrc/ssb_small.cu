@@ -7,8 +7,9 @@
 //      reference's `seen` bitmap), then the presence/frequency extension;
 //   3. ban/allow mask -> -inf (:40-42);
 //   4. max -> PENALTY_OVERFLOW / NO_FINITE_LOGIT (:43-49), NaN -> NON_FINITE_INPUT;
-//   5. greedy: first maximum (:105-108); else scale by the temperature (:73), top-k by radix select on
-//      composite keys, sort the k, softmax in double, top-p, pick (:76-99, sampling.cpp:9-19).
+//   5. greedy: first maximum (:105-108); else scale by the temperature (:73), top-k (k <= 128: the k-th
+//      largest 16-bit key from two histograms, the composites reaching it ranked; otherwise a radix select
+//      on composite keys and a sort of the k), softmax in double, top-p, pick (:76-99, sampling.cpp:9-19).
 #include "ssb_device.cuh"
 #include "ssb_kernels.h"
 
@@ -17,6 +18,8 @@ namespace ssb {
 namespace {
 
 constexpr int kSmallThreads = 512;
+constexpr int kFastK = 128;                // top-k of the histogram path
+constexpr int kFastCand = kSmallThreads;   // candidates it ranks (one per thread); more take the general path
 
 template <typename TIn, bool kDebug>
 __global__ void __launch_bounds__(kSmallThreads) small_rows_kernel(const SmallArgs a) {
@@ -122,8 +125,59 @@ __global__ void __launch_bounds__(kSmallThreads) small_rows_kernel(const SmallAr
         return;
     }
 
-    // ---- top-k by radix select, then sort the k (s_cnt's space is reused for the candidates)
     const int k = p.k;
+    const double u = a.u ? a.u[row] : 0.0;
+    if (k <= kFastK) {
+        // ---- top-k by the k-th largest 16-bit key (two 256-bin histograms: high byte, then low byte), the
+        // composites whose key reaches it (the k best and their ties at 16 bits), ranked (s_cnt's space)
+        __shared__ __align__(16) uint32_t s_h1[256];
+        __shared__ __align__(16) uint32_t s_h2[256];
+        __shared__ int s_nc;
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) s_h1[i] = 0, s_h2[i] = 0;
+        if (threadIdx.x == 0) s_nc = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < vocab; i += blockDim.x) red_bin(s_h1, true, order_key(s_val[i]) >> 24);
+        __syncthreads();
+        uint32_t above1 = 0;
+        const int b1 = top_bin(s_h1, (uint32_t) k, &above1);  // the histogram holds vocab >= k keys
+        for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+            const uint32_t key = order_key(s_val[i]) >> 16;
+            red_bin(s_h2, (int) (key >> 8) == b1, key & 255u);
+        }
+        __syncthreads();
+        uint32_t above2 = 0;
+        const int b2 = top_bin(s_h2, (uint32_t) k - above1, &above2);
+        const uint32_t P = ((uint32_t) b1 << 8) | (uint32_t) (b2 < 0 ? 0 : b2);
+        uint64_t * s_c = reinterpret_cast<uint64_t *>(s_after);  // [kFastCand] candidates, then draw scratch
+        uint64_t * s_sorted = s_c + kFastCand;                    // [k]
+        for (int base = 0; base < vocab; base += blockDim.x) {  // warp-uniform trip count
+            const int i = base + threadIdx.x;
+            const bool take = i < vocab && (order_key(s_val[i]) >> 16) >= P;
+            const unsigned m = __ballot_sync(0xffffffffu, take);
+            if (m) {
+                int at = 0;
+                if (lane_id() == __ffs(m) - 1) at = atomicAdd(&s_nc, __popc(m));
+                at = __shfl_sync(0xffffffffu, at, __ffs(m) - 1) + __popc(m & ((1u << lane_id()) - 1));
+                if (take && at < kFastCand) s_c[at] = composite(s_val[i], (uint32_t) i);
+            }
+        }
+        __syncthreads();
+        const int nc = s_nc;
+        if (nc <= kFastCand) {  // block-uniform
+            if ((int) threadIdx.x < nc) {
+                const uint64_t mine = s_c[threadIdx.x];
+                int rank = 0;
+                for (int j = 0; j < nc; j++) rank += s_c[j] > mine;
+                if (rank < k) s_sorted[rank] = mine;
+            }
+            __syncthreads();
+            if (warp_id() == 0) draw_row(s_sorted, k, p, u, reinterpret_cast<double *>(s_c), out);
+            return;
+        }
+        __syncthreads();  // too many ties at the bound: the general path below
+    }
+
+    // ---- top-k by radix select, then sort the k (s_cnt's space is reused for the candidates)
     radix_select(vocab, k, [&](int i) { return composite(s_val[i], (uint32_t) i); }, sel);
     const int kp2 = next_pow2(k);
     uint64_t * s_cand = reinterpret_cast<uint64_t *>(s_after);      // [kp2]
@@ -147,7 +201,6 @@ __global__ void __launch_bounds__(kSmallThreads) small_rows_kernel(const SmallAr
     }
     __syncthreads();
     bitonic_sort_desc(s_cand, kp2);
-    const double u = a.u ? a.u[row] : 0.0;
     if (warp_id() == 0) draw_row(s_cand, k, p, u, s_w, out);
 }
 
@@ -166,7 +219,9 @@ size_t small_smem_bytes(int vocab, int k_bound) {
     const size_t vals = ((size_t) vocab * 4 + 15) & ~(size_t) 15;
     const int kp2 = next_pow2(k_bound < 1 ? 1 : k_bound);
     const size_t cnt = (size_t) vocab * 4;
-    const size_t cand = (size_t) kp2 * 8 + (size_t) k_bound * 8;
+    size_t cand = (size_t) kp2 * 8 + (size_t) k_bound * 8;
+    const size_t fast = (size_t) (kFastCand + kFastK) * 8;  // the histogram path's candidates and sorted k
+    cand = cand > fast ? cand : fast;
     return vals + (cnt > cand ? cnt : cand);
 }
 

@@ -294,7 +294,7 @@ def test_statuses(engine, vocab):
     assert list(st) == [ss.ROW_TEMPERATURE_OVERFLOW] * 2
 
 
-@pytest.mark.parametrize("vocab", [100, 151936])
+@pytest.mark.parametrize("vocab", [100, 3072, 151936])  # 3072: more than 512 ties at the small kernel's bound
 def test_ties_lowest_index(engine, oracle, vocab):
     x = np.zeros((3, vocab), np.float32)
     x[0, [11, 7, 99 % vocab]] = 1.0
