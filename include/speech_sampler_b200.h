@@ -160,6 +160,16 @@ SSB_API ssb_status ssb_candidates_rows(ssb_context *ctx, const ssb_rows *rows, i
                                        double *weights, int32_t *count, float *processed, void *stream);
 
 /*
+ * The restricted logits alone, the reference's restricted() (qwen3-tts/sampler.cpp:29-51) for a batch:
+ * the repetition penalty (and the presence/frequency extension) over each row's distinct history ids,
+ * then the mask (-inf where banned / not allowed), before the temperature, into out (f32, row r at
+ * out + r * out_ld, out_ld >= vocab). Reads logits, ld, rows, vocab, dtype, params / row_params,
+ * history* and mask*; ids, status and u are not used (may be null). History ids outside [0, vocab)
+ * are ignored. history_ld is at most SSB_MAX_STREAM_HISTORY. Asynchronous on `stream`.
+ */
+SSB_API ssb_status ssb_restrict_rows(ssb_context *ctx, const ssb_rows *rows, float *out, int64_t out_ld, void *stream);
+
+/*
  * sample() for HOST buffers, as the reference's call sites hold them (a logits readback, a history
  * vector, a ban list): copies the inputs to context-owned device buffers, samples, copies ids and
  * status back and waits for the stream. Pointers in `rows` are HOST pointers here.

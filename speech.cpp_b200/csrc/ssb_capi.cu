@@ -403,6 +403,40 @@ ssb_status ssb_candidates_rows(ssb_context * ctx, const ssb_rows * rows, int32_t
     return run(ctx, rows, &dbg, static_cast<cudaStream_t>(stream));
 }
 
+ssb_status ssb_restrict_rows(ssb_context * ctx, const ssb_rows * r, float * out, int64_t out_ld, void * stream) {
+    if (!r) return fail(SSB_INVALID_ARGUMENT, "rows is null");
+    if (r->rows < 0) return fail(SSB_INVALID_ARGUMENT, "rows is negative");
+    if (r->vocab < 1) return fail(SSB_INVALID_ARGUMENT, "vocab must be at least 1");
+    if (r->vocab > SSB_MAX_VOCAB) return fail(SSB_OUT_OF_RANGE, "vocab exceeds SSB_MAX_VOCAB (16777216)");
+    if (r->ld < r->vocab) return fail(SSB_INVALID_ARGUMENT, "ld is smaller than vocab");
+    if (r->dtype != SSB_F32 && r->dtype != SSB_BF16) return fail(SSB_INVALID_ARGUMENT, "dtype is neither SSB_F32 nor SSB_BF16");
+    if (r->mask_kind < SSB_MASK_NONE || r->mask_kind > SSB_MASK_ALLOW) return fail(SSB_INVALID_ARGUMENT, "mask_kind is not an ssb_mask_kind");
+    if (r->reserved != 0 || r->params.reserved != 0) return fail(SSB_INVALID_ARGUMENT, "reserved fields must be 0");
+    if (!ctx) return fail(SSB_INVALID_ARGUMENT, "ctx is null");
+    if (r->rows == 0) return ok();
+    if (!r->logits) return fail(SSB_INVALID_ARGUMENT, "logits is null");
+    if (!out) return fail(SSB_INVALID_ARGUMENT, "out is null");
+    if (out_ld < r->vocab) return fail(SSB_INVALID_ARGUMENT, "out_ld is smaller than vocab");
+    if (r->mask_kind != SSB_MASK_NONE) {
+        if (!r->mask) return fail(SSB_INVALID_ARGUMENT, "mask_kind is set but mask is null");
+        if (r->mask_ld < 0) return fail(SSB_INVALID_ARGUMENT, "mask_ld is negative");
+        if (r->mask_ld > 0 && r->mask_ld < div_up(r->vocab, 32)) return fail(SSB_INVALID_ARGUMENT, "mask_ld is smaller than ceil(vocab / 32)");
+    }
+    int hist_slots = 0;
+    if (r->history) {
+        if (r->history_ld < 0) return fail(SSB_INVALID_ARGUMENT, "history_ld is negative");
+        if (r->history_ld > SSB_MAX_STREAM_HISTORY) return fail(SSB_OUT_OF_RANGE, "history_ld exceeds SSB_MAX_STREAM_HISTORY (8192)");
+        hist_slots = r->history_ld > 0 ? ssb::next_pow2((int) std::max<int64_t>(4, 2 * r->history_ld)) : 0;
+    }
+    ssb_status s = use_device(ctx);
+    if (s != SSB_OK) return s;
+    ssb::RowsArgs a = rows_args(r, 1, nullptr);
+    const cudaError_t e = ssb::launch_restrict(a, hist_slots, r->dtype == SSB_BF16, out, out_ld, ctx->sm_count,
+                                               static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "restrict launch");
+    return ok();
+}
+
 ssb_status ssb_sample_host(ssb_context * ctx, const ssb_rows * rows, void * stream_ptr) {
     Plan plan{};
     ssb_status s = check_rows(rows, false, &plan);

@@ -91,4 +91,10 @@ int nucleus_threads();
 int nucleus_blocks_per_sm(bool bf16, size_t smem);
 cudaError_t launch_nucleus(const NucleusArgs & a, int grid, bool bf16, bool debug, cudaStream_t stream);
 
+// The restricted logits alone (ssb_restrict.cu): every column widened to f32 with the mask applied,
+// then each row's history tokens penalized over it. `a` needs no ids, status or u.
+size_t restrict_smem_bytes(int hist_slots);
+cudaError_t launch_restrict(const RowsArgs & a, int hist_slots, bool bf16, float * out, int64_t out_ld, int sm_count,
+                            cudaStream_t stream);
+
 }  // namespace ssb

@@ -109,6 +109,8 @@ def load_library(path: str = LIB_PATH):
     lib.ssb_candidates_rows.argtypes = [vp, ctypes.POINTER(Rows), i32, vp, vp, vp, vp, vp]
     lib.ssb_sample_host.restype = ctypes.c_int
     lib.ssb_sample_host.argtypes = [vp, ctypes.POINTER(Rows), vp]
+    lib.ssb_restrict_rows.restype = ctypes.c_int
+    lib.ssb_restrict_rows.argtypes = [vp, ctypes.POINTER(Rows), vp, ctypes.c_int64, vp]
     _LIB = lib
     return lib
 
@@ -221,6 +223,21 @@ class Sampler:
         _check(self.lib, self.lib.ssb_candidates_rows(self.ctx, ctypes.byref(r), cap, _dptr(tokens), _dptr(weights),
                                                      _dptr(count), _dptr(proc), s))
         return ids, status, tokens, weights, count, proc
+
+    def restrict(self, logits, p: Params | None = None, history=None, history_len=None, mask=None,
+                 mask_kind=MASK_NONE, row_params=None, out=None, stream=None):
+        """The restricted logits (penalties and mask, before the temperature) as f32 [B, V] on the
+        device: the reference's restricted() for a batch (ssb_restrict_rows)."""
+        import torch
+        b, v = logits.shape
+        if out is None:
+            out = torch.empty((b, v), dtype=torch.float32, device=logits.device)
+        elif out.dtype != torch.float32 or out.shape[0] != b or out.shape[1] < v or out.stride(1) != 1:
+            raise ValueError("out must be float32 [B, >= V] with contiguous rows")
+        r = self._rows_struct(logits, p, history, history_len, mask, mask_kind, None, None, None, row_params)
+        s = None if stream is None else ctypes.c_void_p(stream.cuda_stream)
+        _check(self.lib, self.lib.ssb_restrict_rows(self.ctx, ctypes.byref(r), _dptr(out), out.stride(0), s))
+        return out
 
     def sample_host(self, logits, p: Params | None = None, history=None, history_len=None, mask=None,
                     mask_kind=MASK_NONE, u=None, row_params=None, max_top_k=0, ids=None, status=None, stream=None):

@@ -3,7 +3,7 @@ LM head leaves its logits that way) and every GPU must end with the same token i
 single-GPU engine draws from the whole row.
 
 Protocol, per row (B = 1, the decode step of one stream):
-  1. each rank restricts its own columns through the engine's candidate export (ssb_candidates_rows):
+  1. each rank restricts its own columns through the engine's restricted-logits call (ssb_restrict_rows):
      the repetition penalty and the presence/frequency extension over the history ids that fall in its
      slice (translated to slice columns), the ban/allow mask words of its slice, nothing else. Those
      are per-column operations (qwen3-tts/sampler.cpp:29-51), so every restricted logit equals the one
@@ -50,13 +50,14 @@ def local_mask(mask, off: int, width: int):
     return mask[:, w0:w0 + (width + 31) // 32].contiguous()
 
 
-def restrict_slice(sampler, logits_slice, off: int, p, history=None, mask=None, mask_kind=ss.MASK_NONE, u=None):
-    """Step 1: the restricted logits [1, width] (fp32) of this rank's slice."""
+def restrict_slice(sampler, logits_slice, off: int, p, history=None, mask=None, mask_kind=ss.MASK_NONE, u=None,
+                   out=None):
+    """Step 1: the restricted logits [1, width] (fp32) of this rank's slice (ssb_restrict_rows; `out` may
+    be a [1, >= width] f32 view to write them into)."""
     width = logits_slice.shape[1]
     h = None if history is None else local_history(history, off, width)
     m = None if mask is None or mask_kind == ss.MASK_NONE else local_mask(mask, off, width)
-    _, _, _, _, _, proc = sampler.candidates(logits_slice, p, h, None, m, mask_kind, u, cap=0, processed=True)
-    return proc
+    return sampler.restrict(logits_slice, p, h, None, m, mask_kind, out=out)
 
 
 def assemble(slices, bounds, vocab: int):
@@ -87,10 +88,9 @@ def sample_vocab_sharded(sampler, logits_slice, vocab: int, p, history=None, mas
     off, width = bounds[rank]
     if logits_slice.shape != (1, width):
         raise ValueError(f"rank {rank} holds {tuple(logits_slice.shape)}, its slice is (1, {width})")
-    proc = restrict_slice(sampler, logits_slice, off, p, history, mask, mask_kind, u)
     wmax = max(w for _, w in bounds)
-    padded = torch.full((1, wmax), float("-inf"), dtype=torch.float32, device=proc.device)
-    padded[:, :width] = proc
+    padded = torch.full((1, wmax), float("-inf"), dtype=torch.float32, device=logits_slice.device)
+    restrict_slice(sampler, logits_slice, off, p, history, mask, mask_kind, u, out=padded)
     gathered = [torch.empty_like(padded) for _ in range(world)]
     dist.all_gather(gathered, padded, group=group)
     return sample_whole(sampler, assemble(gathered, bounds, vocab), p, u)

@@ -87,12 +87,16 @@ class _OracleSampler:
         self.o = Oracle()
         self.p = params(**kw)
 
-    def candidates(self, logits, p, history, history_len, mask, mask_kind, u, cap=0, processed=True):
+    def restrict(self, logits, p, history, history_len, mask, mask_kind, out=None):
         import torch
         h = None if history is None else history.numpy()[0]
         m = None if mask is None else mask.numpy().view(np.uint32)[0]
-        r = self.o.sample_row(logits.numpy()[0], self.p, h, m, mask_kind, float(u[0]), want_processed=True)
-        return None, None, None, None, None, torch.from_numpy(r["processed"].copy()).view(1, -1)
+        r = self.o.sample_row(logits.numpy()[0], self.p, h, m, mask_kind, 0.5, want_processed=True)
+        proc = torch.from_numpy(r["processed"].copy()).view(1, -1)
+        if out is None:
+            return proc
+        out[:, :proc.shape[1]] = proc
+        return out
 
     def sample(self, row, p, history, history_len, mask, mask_kind, u):
         import torch
