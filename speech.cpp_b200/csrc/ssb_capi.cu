@@ -249,6 +249,9 @@ ssb_status run(ssb_context * ctx, const ssb_rows * r, const Debug * dbg, cudaStr
     const int slots = std::min(ctx->max_slots, ctx->sm_count * occ);
     const int min_chunk = mode == 0 ? 2048 : 4096;
     int64_t splits = std::max<int64_t>(1, std::min<int64_t>(div_up(r->vocab, min_chunk), slots / std::max(1, r->rows)));
+    // two halves of a row do not pay for their merge in the top-k kernel: one CTA per row streams the
+    // whole row instead (128 rows of 151936 bf16: 22.8 us against 24.7 us split in two)
+    if (use_topk && splits == 2) splits = 1;
     splits = std::max<int64_t>(splits, div_up(r->vocab, max_chunk));
     int64_t chunk = div_up(div_up(r->vocab, splits), 32) * 32;
     splits = div_up(r->vocab, chunk);

@@ -173,6 +173,9 @@ extern "C" ssb_status ssb_sample_rows_noalloc(const ssb_rows * r, void * stream_
     const int slots = std::min(kScratchSlots, d->sm_count * occ);
     const int min_chunk = all_greedy ? 2048 : 4096;
     int64_t splits = std::max<int64_t>(1, std::min<int64_t>(div_up(r->vocab, min_chunk), slots / std::max(1, r->rows)));
+    // two halves of a row do not pay for their merge in the top-k kernel: one CTA per row streams the
+    // whole row instead (128 rows of 151936 bf16: 22.8 us against 24.7 us split in two)
+    if (splits == 2) splits = 1;
     splits = std::max<int64_t>(splits, div_up(r->vocab, max_chunk));
     const int64_t chunk = div_up(div_up(r->vocab, splits), 32) * 32;
     splits = div_up(r->vocab, chunk);
