@@ -53,9 +53,6 @@ __global__ void __launch_bounds__(kSmallThreads) small_rows_kernel(const SmallAr
     uint32_t * s_cnt = reinterpret_cast<uint32_t *>(s_after);               // [vocab], aliased below
 
     const TIn * src = reinterpret_cast<const TIn *>(a.logits) + (int64_t) row * a.ld;
-    for (int i = threadIdx.x; i < vocab; i += blockDim.x) s_val[i] = Elem<TIn>::load1(src, i);
-
-    // ---- penalties over the history
     const int32_t * hist = a.history ? a.history + (int64_t) row * a.history_ld : nullptr;
     int hlen = 0;
     if (hist) {
@@ -63,11 +60,28 @@ __global__ void __launch_bounds__(kSmallThreads) small_rows_kernel(const SmallAr
         hlen = hlen < 0 ? 0 : (hlen > (int) a.history_ld ? (int) a.history_ld : hlen);
     }
     const bool penal = p.history_applies && hlen > 0;
+    // each thread's first history id is requested with the logits, eight of which are in flight per thread
+    const int32_t h_first = penal && (int) threadIdx.x < hlen ? __ldg(hist + threadIdx.x) : -1;
+    for (int base = 0; base < vocab; base += 8 * kSmallThreads) {
+        float v[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            const int i = base + q * kSmallThreads + (int) threadIdx.x;
+            v[q] = i < vocab ? Elem<TIn>::load1(src, i) : 0.0f;
+        }
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            const int i = base + q * kSmallThreads + (int) threadIdx.x;
+            if (i < vocab) s_val[i] = v[q];
+        }
+    }
+
+    // ---- penalties over the history
     if (penal) {
         for (int i = threadIdx.x; i < vocab; i += blockDim.x) s_cnt[i] = 0;
         __syncthreads();
         for (int i = threadIdx.x; i < hlen; i += blockDim.x) {
-            const int32_t t = hist[i];
+            const int32_t t = i == (int) threadIdx.x ? h_first : hist[i];
             if (t >= 0 && t < vocab) atomicAdd(&s_cnt[t], 1u);
         }
     }
