@@ -652,16 +652,31 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
             uint64_t q[QN];
 #pragma unroll
             for (int r = 0; r < QN; r++) q[r] = 0;
-            for (int sp = warp; sp < splits; sp += kConsumerWarps) {
-                const int64_t sl = (int64_t) row * splits + sp;
-                const int n = __ldcg(sa.part_n + sl);
-                uint64_t t[QN];
+            // four lists at a time: their counts and entries requested together (entries up to k_bound, the
+            // slot's own storage, then cut to the count), so a list costs no dependent round trip of its own
+            for (int sp0 = warp; sp0 < splits; sp0 += 4 * kConsumerWarps) {
+                uint64_t t[4][QN];
+                int n[4];
 #pragma unroll
-                for (int r = 0; r < QN; r++) {
-                    const int i = r * 32 + lane;
-                    t[r] = i < n ? __ldcg(reinterpret_cast<const unsigned long long *>(sa.part_cand) + sl * sa.r.k_bound + i) : 0ull;
+                for (int g = 0; g < 4; g++) {
+                    const int sp = sp0 + g * kConsumerWarps;
+                    const int64_t sl = (int64_t) row * splits + sp;
+                    n[g] = sp < splits ? __ldcg(sa.part_n + sl) : 0;
+#pragma unroll
+                    for (int r = 0; r < QN; r++) {
+                        const int i = r * 32 + lane;
+                        t[g][r] = sp < splits && i < sa.r.k_bound
+                                      ? __ldcg(reinterpret_cast<const unsigned long long *>(sa.part_cand) + sl * sa.r.k_bound + i)
+                                      : 0ull;
+                    }
                 }
-                warp_merge_sorted<QN>(q, t);
+#pragma unroll
+                for (int g = 0; g < 4; g++) {
+#pragma unroll
+                    for (int r = 0; r < QN; r++)
+                        if (r * 32 + lane >= n[g]) t[g][r] = 0ull;
+                    if (sp0 + g * kConsumerWarps < splits) warp_merge_sorted<QN>(q, t[g]);  // warp-uniform
+                }
             }
 #pragma unroll
             for (int r = 0; r < QN; r++) lists[warp * 32 * QN + r * 32 + lane] = q[r];
