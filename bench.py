@@ -317,7 +317,7 @@ def main():
         ms = float(t.item())
         dist.barrier()
     ms_per_step = ms / args.steps
-    total_rows = w["total"] if args.scaling == "strong" else rows * world
+    total_rows = rows * world  # the rows every rank sampled (strong scaling drops a remainder of total // world)
     value = total_rows / (ms_per_step * 1e-3)
 
     # ---- end to end through the host-buffer entry point (pinned host memory)

@@ -43,12 +43,17 @@ def params(greedy=False, temperature=1.0, top_k=0, top_p=1.0, repetition_penalty
                   presence_penalty, frequency_penalty, 0)
 
 
+# The reference's source tree (speech.cpp), read only to compile its sampler into _ref/; the
+# SPEECH_REFERENCE environment variable overrides the default location.
+REFERENCE = os.environ.get("SPEECH_REFERENCE", "/root/reference")
+
+
 def build(ref: bool = True) -> None:
     """Builds liboracle.so (and the reference library when its sources are present)."""
     targets = ["oracle"]
-    if ref and os.path.isdir("/root/reference/src"):
+    if ref and os.path.isdir(os.path.join(REFERENCE, "src")):
         targets.append("ref")
-    subprocess.run(["make", "-s", "-C", HERE] + targets, check=True)
+    subprocess.run(["make", "-s", "-C", HERE, f"REF={REFERENCE}"] + targets, check=True)
 
 
 def _p(a, t):

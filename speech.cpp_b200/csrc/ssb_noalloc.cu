@@ -12,8 +12,9 @@
 // fixed-size array in this file, `g_scratch` (kScratchBytes, about 2.03 MiB, held by every GPU that
 // loads the library until the process exits). Host code cannot use the array's name as a device
 // address, so the first call on each device looks the address up with cudaGetSymbolAddress (with that
-// device current) and keeps it; make that first call before any stream capture. The caller still
-// passes every input and output buffer.
+// device current), clears the per-row arrival counters once (a synchronous cudaMemset of that array,
+// not an allocation) and keeps the address; make that first call before any stream capture. The
+// caller still passes every input and output buffer.
 //
 // Limits: rows of more than SSB_SMALL_VOCAB tokens, 16-byte-aligned rows, and top-k of at most 128
 // (or greedy rows) — the rows the top-k kernel (ssb_topk.cu) takes; anything else is refused
@@ -21,9 +22,9 @@
 // ssb_sample_rows launches it; only where its scratch comes from differs.
 //
 // Every call shares the one array: calls that overlap on the GPU (on different streams, or from
-// different threads without ordering) race on it and must not be made. Each call clears the per-row
-// arrival counters it uses before its kernel runs, so a call never depends on what an earlier call
-// left behind.
+// different threads without ordering) race on it and must not be made. The kernel returns each row's
+// arrival counter to zero itself (the last CTA of a row resets it), so a call leaves the array ready for
+// the next one; the counters are cleared once, when the device is set up.
 #include <algorithm>
 #include <cstdint>
 #include <mutex>
@@ -54,6 +55,10 @@ struct DeviceSetup {
     unsigned char * scratch = nullptr;  // g_scratch's device address on this device
     int sm_count = 0;
     int max_smem = 0;  // opt-in shared memory per block
+    // occupancy of the top-k kernel per (warp-list width class, bf16), and the shared memory it was
+    // measured at (measured once per shape, under g_setup_mutex)
+    int occ[3][2] = {};
+    size_t occ_smem[3][2] = {};
 };
 
 DeviceSetup g_setup[kMaxDevices];
@@ -81,6 +86,10 @@ ssb_status setup(int device, DeviceSetup ** out) {
         if (e == cudaSuccess) e = cudaDeviceGetAttribute(&d.max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
         if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
         d.scratch = static_cast<unsigned char *>(p);
+        // the arrival counters start at zero; every launch leaves them at zero again
+        e = cudaMemset(d.scratch + kCandBytes + (size_t) kScratchSlots * 12, 0, (size_t) kScratchSlots * sizeof(uint32_t));
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return cuda_fail(e, "clearing the arrival counters");
         d.ready = true;
     }
     *out = &d;
@@ -164,11 +173,24 @@ extern "C" ssb_status ssb_sample_rows_noalloc(const ssb_rows * r, void * stream_
     sa.hist_slots = r->history ? ssb::next_pow2((int) std::max<int64_t>(4, 2 * r->history_ld)) : 0;
     sa.sel_slots = ssb::next_pow2(std::max(kb, 2));
     const int full_chunk = (int) div_up(r->vocab, 32) * 32;
-    const int max_chunk = std::min(full_chunk, ssb::topk_max_chunk(bf16));
+    // the kernel keeps per-chunk state in shared memory: a long history leaves less of it, so the chunk
+    // is halved until it fits (as ssb_sample_rows does); refused only if even a 4096-column chunk does not
+    int max_chunk = std::min(full_chunk, ssb::topk_max_chunk(bf16));
+    while (max_chunk > 4096 && ssb::topk_smem_bytes(kw, bf16, max_chunk, sa.hist_slots, sa.sel_slots) > (size_t) d->max_smem)
+        max_chunk = (int) div_up(max_chunk / 2, 32) * 32;
     const size_t smem = ssb::topk_smem_bytes(kw, bf16, max_chunk, sa.hist_slots, sa.sel_slots);
     if (smem > (size_t) d->max_smem)
         return fail(SSB_OUT_OF_RANGE, "the history is too long for the top-k kernel's shared memory; use ssb_sample_rows");
-    const int occ = ssb::topk_blocks_per_sm(kw, bf16, smem);
+    const int kwc = kw == 1 ? 0 : (kw == 2 ? 1 : 2);
+    int occ = 0;
+    {
+        std::lock_guard<std::mutex> lock(g_setup_mutex);
+        if (d->occ[kwc][bf16] == 0 || d->occ_smem[kwc][bf16] != smem) {
+            d->occ[kwc][bf16] = ssb::topk_blocks_per_sm(kw, bf16, smem);
+            d->occ_smem[kwc][bf16] = smem;
+        }
+        occ = d->occ[kwc][bf16];
+    }
     if (occ <= 0) return fail(SSB_DEVICE, "the top-k kernel does not fit on this device");
     const int slots = std::min(kScratchSlots, d->sm_count * occ);
     const int min_chunk = all_greedy ? 2048 : 4096;
@@ -190,8 +212,6 @@ extern "C" ssb_status ssb_sample_rows_noalloc(const ssb_rows * r, void * stream_
         sa.part_max = reinterpret_cast<float *>(base + kCandBytes + (size_t) kScratchSlots * 4);
         sa.part_flags = reinterpret_cast<int32_t *>(base + kCandBytes + (size_t) kScratchSlots * 8);
         sa.counters = reinterpret_cast<uint32_t *>(base + kCandBytes + (size_t) kScratchSlots * 12);
-        e = cudaMemsetAsync(sa.counters, 0, (size_t) r->rows * sizeof(uint32_t), stream);
-        if (e != cudaSuccess) return cuda_fail(e, "clearing the arrival counters");
     }
     e = ssb::launch_topk(sa, kw, bf16, false, stream);
     if (e != cudaSuccess) return cuda_fail(e, "top-k kernel launch");

@@ -17,7 +17,14 @@ constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kStreamCtaThreads = kConsumers + 32;  // + the producer warp
 constexpr int kStageGroups = kStageBytes / 16;      // 16-byte groups per stage
 constexpr int kGroupsPerThread = kStageGroups / kConsumers;
-constexpr uint32_t kWaitLimit = 1u << 22;           // bounded mbarrier polls
+// Bounded mbarrier waits: a wait gives up after this many SM clock cycles (about 1 s at 1.9 GHz).
+// The wait-limit test build (SSB_WAIT_TEST) shortens it so that its planted missing stage times out
+// quickly.
+#ifdef SSB_WAIT_TEST
+constexpr long long kWaitCycles = 1ll << 22;
+#else
+constexpr long long kWaitCycles = 1ll << 31;
+#endif
 
 static_assert(kGroupsPerThread * kConsumers * 16 == kStageBytes, "stage must split evenly");
 static_assert(kGroupsPerThread == 4, "a lane holds four groups of a stage");
@@ -38,23 +45,34 @@ __device__ __forceinline__ void mbar_arrive(uint64_t * bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
+// One test of phase `parity` of `bar`; the thread may be suspended (not spinning, so it takes no issue
+// slots from the warps that work meanwhile) until the phase completes or about kSuspendNs pass.
+constexpr uint32_t kSuspendNs = 100000;
 __device__ __forceinline__ bool mbar_try_wait(uint64_t * bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendNs)
         : "memory");
     return ok != 0;
 }
 
-// Waits for phase `parity` of `bar`, giving up after kWaitLimit polls (returns false).
+// Waits for phase `parity` of `bar`, giving up after kWaitCycles clock cycles (returns false).
 __device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity) {
-    for (uint32_t n = 0; n < kWaitLimit; n++)
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (true) {
         if (mbar_try_wait(bar, parity)) return true;
-    return false;
+        if (clock64() - t0 > kWaitCycles) return false;
+    }
+}
+
+// Barrier of `threads` threads (a multiple of 32) on hardware barrier `id` (1..15; 0 is __syncthreads).
+__device__ __forceinline__ void bar_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 // One TMA bulk copy global -> shared, completing on `bar` (both addresses and the size are multiples

@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
     __shared__ SelectState sel;
     __shared__ float s_redf[32];
     __shared__ int s_redi[32];
-    __shared__ int s_count, s_gather, s_abort, s_last, s_n0, s_qn;
+    __shared__ int s_count, s_gather, s_abort, s_last, s_n0, s_qn, s_issued;
     __shared__ __align__(16) uint32_t s_f1[256];  // bound: histogram of the kept keys' high bytes
     __shared__ __align__(16) uint32_t s_f2[256];  // and of their low bytes within the chosen high byte
     __shared__ int s_qlist[kListMax];
@@ -190,11 +190,13 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
         for (int q = 0; q < kTkStages; q++) mbar_init(&s_full[q], 1), mbar_init(&s_empty[q], kConsumerWarps);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        for (int q = 0; q < kTkStages && q < nstages; q++) {
+        int q = 0;
+        for (; q < kTkStages && q < nstages; q++) {
             const uint32_t bytes = (uint32_t) min(kStageBytes, (nvec - q * kStageGroups) * 16);
             mbar_expect(&s_full[q], bytes);
             bulk_load(ring + q * kStageBytes, gsrc + (size_t) q * kStageBytes, bytes, &s_full[q]);
         }
+        s_issued = q;
     }
 
     // ---- special blocks (all threads, while the first stages load)
@@ -285,23 +287,34 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
 #pragma unroll
     for (int j = 0; j < kGroupsPerThread; j++) best_rv[j] = make_uint4(0, 0, 0, 0);
     if (!consumer) {
-        // producer
+        // producer: a slot is refilled once every consumer warp has released it; a release that does not
+        // come within the bounded wait stops the producer (no further copy is issued)
         if (lane == 0) {
-            for (int st = kTkStages; st < nstages; st++) {
+            int st = kTkStages;
+            for (; st < nstages; st++) {
                 const int slot = st % kTkStages;
-                if (!mbar_wait(&s_empty[slot], (uint32_t) ((st / kTkStages) - 1) & 1u)) s_abort = 1;
+                if (!mbar_wait(&s_empty[slot], (uint32_t) ((st / kTkStages) - 1) & 1u)) {
+                    atomicOr(&s_abort, 1);
+                    break;
+                }
+#ifdef SSB_WAIT_TEST
+                // the wait-limit test build: row 0's first refill is never issued, so its consumers'
+                // bounded wait runs out (a stage that nothing fills)
+                if (row == 0 && split == 0 && st == kTkStages) continue;
+#endif
                 const uint32_t bytes = (uint32_t) min(kStageBytes, (nvec - st * kStageGroups) * 16);
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 mbar_expect(&s_full[slot], bytes);
                 bulk_load(ring + slot * kStageBytes, gsrc + (size_t) st * kStageBytes, bytes, &s_full[slot]);
             }
+            if (st > kTkStages) s_issued = st;
         }
     } else {
         int slot = 0;
         uint32_t phase = 0;
         for (int st = 0; st < nstages; st++) {
             const uint4 * stage = reinterpret_cast<const uint4 *>(ring + slot * kStageBytes);
-            if (!mbar_wait(&s_full[slot], phase)) s_abort = 1;
+            if (!mbar_wait(&s_full[slot], phase)) atomicOr(&s_abort, 1);
             const int sgroups = min(kStageGroups, nvec - st * kStageGroups);
             uint4 rv[kGroupsPerThread];
 #pragma unroll
@@ -345,6 +358,13 @@ __global__ void __launch_bounds__(kTkThreads, 2) topk_rows_kernel(const StreamAr
     red_bin(s_f1, consumer && key0 != 0, key0 >> 8);
     red_bin(s_f1, consumer && key1 != 0, key1 >> 8);
     __syncthreads();
+    if (tid == 0 && s_abort) {
+        // a wait ran out: before the ring's memory is reused (and before the CTA exits), wait (bounded)
+        // for the last copy issued into every slot
+        const int issued = s_issued;
+        for (int st = issued - kTkStages; st < issued; st++)
+            if (st >= 0) (void) mbar_wait(&s_full[st % kTkStages], (uint32_t) (st / kTkStages) & 1u);
+    }
     uint32_t above1 = 0;
     const int b1 = top_bin(s_f1, (uint32_t) k, &above1);
     red_bin(s_f2, consumer && b1 >= 0 && key0 != 0 && (int) (key0 >> 8) == b1, key0 & 255u);

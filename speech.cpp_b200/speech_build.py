@@ -1,6 +1,11 @@
 """Builds libspeech_sampler_b200.so in-tree: every csrc/*.cu for sm_100a with nvcc, linked with the
 static CUDA runtime and hidden visibility except the C ABI of include/speech_sampler_b200.h.
 
+Also builds the wait-limit test library, libspeech_sampler_b200_waittest.so: the same sources with
+SSB_WAIT_TEST defined, whose bounded waits give up after about 2 ms and whose top-k kernel never
+issues one refill of row 0 (a stage that nothing fills), so that a test can check that a wait that runs
+out becomes SSB_ROW_DEVICE_TIMEOUT without a fault or a hang. It is test infrastructure only.
+
     python speech.cpp_b200/speech_build.py          # incremental
     python speech.cpp_b200/speech_build.py --force  # rebuild everything
 """
@@ -18,6 +23,8 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 OBJ = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libspeech_sampler_b200.so")
+OBJ_WAITTEST = os.path.join(PKG, "_build_waittest")
+LIB_WAITTEST = os.path.join(PKG, "libspeech_sampler_b200_waittest.so")
 INCLUDE = os.path.join(ROOT, "include")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -49,17 +56,19 @@ def _stale(target: str, deps) -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> str:
-    os.makedirs(OBJ, exist_ok=True)
+def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False, waittest: bool = False) -> str:
+    objdir, lib = (OBJ_WAITTEST, LIB_WAITTEST) if waittest else (OBJ, LIB)
+    os.makedirs(objdir, exist_ok=True)
     cc = nvcc()
     hdrs = headers()
     jobs = []
+    extra = ["-DSSB_WAIT_TEST"] if waittest else []
     for src in sources():
-        obj = os.path.join(OBJ, os.path.basename(src)[:-3] + ".o")
+        obj = os.path.join(objdir, os.path.basename(src)[:-3] + ".o")
         if force or ptxas_info or _stale(obj, [src] + hdrs):
-            cmd = [cc] + NVCC_FLAGS + (["-Xptxas", "-v"] if ptxas_info else []) + ["-c", src, "-o", obj]
+            cmd = [cc] + NVCC_FLAGS + extra + (["-Xptxas", "-v"] if ptxas_info else []) + ["-c", src, "-o", obj]
             jobs.append((src, cmd))
-    objs = [os.path.join(OBJ, os.path.basename(s)[:-3] + ".o") for s in sources()]
+    objs = [os.path.join(objdir, os.path.basename(s)[:-3] + ".o") for s in sources()]
 
     def run(job):
         src, cmd = job
@@ -76,12 +85,12 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
                     raise RuntimeError(f"nvcc failed on {src}")
                 if ptxas_info or verbose:
                     sys.stderr.write(r.stderr)
-    if force or jobs or _stale(LIB, objs):
-        cmd = [cc] + ARCH + ["-shared", "-cudart", "static", "-o", LIB] + objs + ["-lpthread"]
+    if force or jobs or _stale(lib, objs):
+        cmd = [cc] + ARCH + ["-shared", "-cudart", "static", "-o", lib] + objs + ["-lpthread"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
-    return LIB
+    return lib
 
 
 if __name__ == "__main__":
@@ -91,3 +100,4 @@ if __name__ == "__main__":
     ap.add_argument("--ptxas-info", action="store_true")
     args = ap.parse_args()
     print(build(force=args.force, verbose=args.verbose, ptxas_info=args.ptxas_info))
+    print(build(force=args.force, verbose=args.verbose, waittest=True))

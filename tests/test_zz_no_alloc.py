@@ -1,10 +1,11 @@
 """ssb_sample_rows_noalloc — sampling for callers that cannot allocate device memory (a runtime that
 owns every device buffer through its own pool, or a decode loop that must not call cudaMalloc). It
 uses a fixed scratch array inside the library instead of a context's allocations, so its answers must
-be exactly those of ssb_sample_rows (token ids and statuses are integers: the tolerance is zero), on
-two calls in a row (the shared array keeps the previous call's contents). This file is collected last
-so that a run stopping at the first failure has run every other test; it also passes alone in a
-fresh process, where its first call performs the per-device set-up."""
+be exactly those of ssb_sample_rows, and those of the oracle restatement (token ids and statuses are
+integers: the tolerance is zero), on two calls in a row (the shared array keeps the previous call's
+contents). This file is collected last so that a run stopping at the first failure has run every
+other test; it also passes alone in a fresh process, where its first call performs the per-device
+set-up."""
 import ctypes
 
 import numpy as np
@@ -12,6 +13,7 @@ import pytest
 
 import speech_sampler as ss
 import speech_workloads as wl
+from oracle import Oracle, params as oparams
 
 pytestmark = pytest.mark.gpu
 
@@ -47,6 +49,7 @@ def test_noalloc_matches_sample_rows_twice():
     lib = ss.load_library()
     noalloc = _noalloc(lib)
     sampler = ss.Sampler(0)
+    oracle = Oracle()
     try:
         for name, x, p, hist, mask, kind, u in _cases():
             xt = torch.from_numpy(x)
@@ -56,6 +59,10 @@ def test_noalloc_matches_sample_rows_twice():
             uu = None if u is None else torch.from_numpy(u).cuda()
             want_ids, want_st = sampler.sample(xt, p, h, None, m, kind, uu)
             torch.cuda.synchronize()
+            op = oparams(greedy=bool(p.greedy), temperature=p.temperature, top_k=p.top_k, top_p=p.top_p,
+                         repetition_penalty=p.repetition_penalty, presence_penalty=p.presence_penalty,
+                         frequency_penalty=p.frequency_penalty)
+            o_ids, o_st, _ = oracle.sample_rows(x, op, history=hist, mask=mask, mask_kind=kind, u=u)
             for call in range(2):
                 ids = torch.full((x.shape[0],), -7, dtype=torch.int32, device="cuda")
                 st = torch.full((x.shape[0],), -7, dtype=torch.int32, device="cuda")
@@ -65,6 +72,7 @@ def test_noalloc_matches_sample_rows_twice():
                 torch.cuda.synchronize()
                 assert torch.equal(ids, want_ids), (name, call)
                 assert torch.equal(st, want_st), (name, call)
+                assert np.array_equal(ids.cpu().numpy(), o_ids) and np.array_equal(st.cpu().numpy(), o_st), (name, call)
     finally:
         sampler.close()
 
