@@ -69,11 +69,28 @@ typedef enum ssb_dtype { SSB_F32 = 0, SSB_BF16 = 1 } ssb_dtype;
 typedef enum ssb_mask_kind { SSB_MASK_NONE = 0, SSB_MASK_BAN = 1, SSB_MASK_ALLOW = 2 } ssb_mask_kind;
 
 /*
+ * The family whose candidate rule a row follows. Every family takes the restricted logits (penalties,
+ * then the mask) and draws with pick() (src/common/sampling.cpp:9-19).
+ *   QWEN3_TTS  candidates()/sample(), src/families/qwen3-tts/sampler.cpp:69-111 (the default)
+ *   HARU       haru::candidates(), src/families/haru/sampler.cpp:18-61: float32 softmax, a temperature of
+ *              0 or less (or greedy) draws the first maximum, top_k 0 or >= vocab keeps every token,
+ *              top-p gives 0 weight to the tokens past it; NaN or +inf -> SSB_ROW_NON_FINITE_INPUT
+ *   DRAMA3     drama3::candidates(), src/families/drama3/sampler.cpp:30-58: temperature at least 1e-5,
+ *              top_k at least 1, the softmax over every token, the token that passes top_p dropped; any
+ *              non-finite logit -> SSB_ROW_NON_FINITE_INPUT
+ * HARU and DRAMA3 keep at most 4096 candidates: a larger effective top-k is refused (SSB_OUT_OF_RANGE;
+ * SSB_ROW_INVALID_ROW for a row of row_params), and every row of a call must have the call's family.
+ */
+typedef enum ssb_flavor { SSB_FLAVOR_QWEN3_TTS = 0, SSB_FLAVOR_HARU = 1, SSB_FLAVOR_DRAMA3 = 2 } ssb_flavor;
+
+/*
  * Sampling settings of one row. The first five fields are the reference's SamplingParams
  * (src/families/qwen3-tts/sampler.h:12-24) with the same meaning and defaults
  * {greedy 0, temperature 1, top_k 0 (= every token), top_p 1, repetition_penalty 1}. The penalties
  * after them are extensions (0 = off): for each distinct in-range history id with c occurrences,
  * after the repetition penalty, l = l - frequency_penalty * c; l = l - presence_penalty (fp32).
+ * Haru's and Drama 3's Sampling {temperature, top_k, top_p} (haru/sampler.h:13-19,
+ * drama3/sampler.h:12-17) map onto the same fields with `flavor` set.
  */
 typedef struct ssb_params {
     int32_t greedy;
@@ -83,7 +100,7 @@ typedef struct ssb_params {
     float repetition_penalty;
     float presence_penalty;
     float frequency_penalty;
-    int32_t reserved; /* must be 0 */
+    int32_t flavor; /* ssb_flavor (0: Qwen3-TTS) */
 } ssb_params;
 
 /*

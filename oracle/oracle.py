@@ -34,7 +34,7 @@ class Params(ctypes.Structure):
     _fields_ = [("greedy", ctypes.c_int32), ("temperature", ctypes.c_float), ("top_k", ctypes.c_int32),
                 ("top_p", ctypes.c_float), ("repetition_penalty", ctypes.c_float),
                 ("presence_penalty", ctypes.c_float), ("frequency_penalty", ctypes.c_float),
-                ("reserved", ctypes.c_int32)]
+                ("flavor", ctypes.c_int32)]
 
 
 def params(greedy=False, temperature=1.0, top_k=0, top_p=1.0, repetition_penalty=1.0,
@@ -89,11 +89,12 @@ class Oracle:
         lib.oracle_pick.argtypes = [ctypes.POINTER(ctypes.c_double), ctypes.c_int32, ctypes.c_double]
         lib.oracle_uniform.restype = None
         lib.oracle_uniform.argtypes = [ctypes.c_uint64, ctypes.c_int64, ctypes.POINTER(ctypes.c_double)]
-        lib.oracle_haru_candidates.restype = ctypes.c_int
-        lib.oracle_haru_candidates.argtypes = [ctypes.POINTER(ctypes.c_float), ctypes.c_int32, ctypes.c_float,
-                                               ctypes.c_int32, ctypes.c_float, ctypes.POINTER(ctypes.c_int32),
-                                               ctypes.POINTER(ctypes.c_double), ctypes.c_int32,
-                                               ctypes.POINTER(ctypes.c_int32)]
+        for name in ("oracle_haru_candidates", "oracle_drama3_candidates"):
+            f = getattr(lib, name)
+            f.restype = ctypes.c_int
+            f.argtypes = [ctypes.POINTER(ctypes.c_float), ctypes.c_int32, ctypes.c_float, ctypes.c_int32,
+                          ctypes.c_float, ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_double),
+                          ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)]
 
     def sample_row(self, logits, p: Params, history=None, mask=None, mask_kind=MASK_NONE, u=0.0, cap=0,
                    want_processed=False):
@@ -148,17 +149,24 @@ class Oracle:
         self.lib.oracle_uniform(seed, n, _p(out, ctypes.c_double))
         return out
 
-    def haru_candidates(self, logits, temperature, top_k, top_p, cap=None):
+    def _family(self, f, logits, temperature, top_k, top_p, cap):
         x = np.ascontiguousarray(logits, dtype=np.float32)
         cap = len(x) if cap is None else cap
-        tokens = np.empty(cap, np.int32)
-        weights = np.empty(cap, np.float64)
+        tokens = np.empty(max(cap, 1), np.int32)
+        weights = np.empty(max(cap, 1), np.float64)
         count = ctypes.c_int32(0)
-        st = self.lib.oracle_haru_candidates(_p(x, ctypes.c_float), len(x), temperature, top_k, top_p,
-                                             _p(tokens, ctypes.c_int32), _p(weights, ctypes.c_double), cap,
-                                             ctypes.byref(count))
+        st = f(_p(x, ctypes.c_float), len(x), temperature, top_k, top_p, _p(tokens, ctypes.c_int32),
+               _p(weights, ctypes.c_double), cap, ctypes.byref(count))
         c = min(count.value, cap)
         return st, tokens[:c].copy(), weights[:c].copy()
+
+    def haru_candidates(self, logits, temperature, top_k, top_p, cap=None):
+        """haru::candidates (haru/sampler.cpp:18-61): (status, tokens, weights)."""
+        return self._family(self.lib.oracle_haru_candidates, logits, temperature, top_k, top_p, cap)
+
+    def drama3_candidates(self, logits, temperature, top_k, top_p, cap=None):
+        """drama3::candidates (drama3/sampler.cpp:30-60): (status, tokens, weights)."""
+        return self._family(self.lib.oracle_drama3_candidates, logits, temperature, top_k, top_p, cap)
 
 
 class RefSampler:
@@ -181,9 +189,11 @@ class RefSampler:
         lib.ref_pick.argtypes = [f64p, ctypes.c_int32, ctypes.c_double]
         lib.ref_uniform.restype = None
         lib.ref_uniform.argtypes = [ctypes.c_uint64, ctypes.c_int64, f64p]
-        lib.ref_haru_candidates.restype = ctypes.c_int
-        lib.ref_haru_candidates.argtypes = [f32p, ctypes.c_int32, ctypes.c_float, ctypes.c_int32, ctypes.c_float,
-                                            i32p, f64p, ctypes.c_int32, i32p]
+        for name in ("ref_haru_candidates", "ref_drama3_candidates"):
+            f = getattr(lib, name)
+            f.restype = ctypes.c_int
+            f.argtypes = [f32p, ctypes.c_int32, ctypes.c_float, ctypes.c_int32, ctypes.c_float, i32p, f64p,
+                          ctypes.c_int32, i32p]
         lib.ref_time_rows.restype = ctypes.c_double
         lib.ref_time_rows.argtypes = [f32p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int64, ctypes.POINTER(Params),
                                       i32p, ctypes.c_int64, i32p, u8p, ctypes.c_int64, f64p, ctypes.c_int32,
@@ -230,16 +240,10 @@ class RefSampler:
         return out
 
     def haru_candidates(self, logits, temperature, top_k, top_p, cap=None):
-        x = np.ascontiguousarray(logits, dtype=np.float32)
-        cap = len(x) if cap is None else cap
-        tokens = np.empty(cap, np.int32)
-        weights = np.empty(cap, np.float64)
-        count = ctypes.c_int32(0)
-        st = self.lib.ref_haru_candidates(_p(x, ctypes.c_float), len(x), temperature, top_k, top_p,
-                                          _p(tokens, ctypes.c_int32), _p(weights, ctypes.c_double), cap,
-                                          ctypes.byref(count))
-        c = min(count.value, cap)
-        return st, tokens[:c].copy(), weights[:c].copy()
+        return Oracle._family(self, self.lib.ref_haru_candidates, logits, temperature, top_k, top_p, cap)
+
+    def drama3_candidates(self, logits, temperature, top_k, top_p, cap=None):
+        return Oracle._family(self, self.lib.ref_drama3_candidates, logits, temperature, top_k, top_p, cap)
 
     def time_rows(self, logits_f32, p: Params, history=None, hlens=None, banned=None, u=None, threads=1):
         """sample() over every row with `threads` workers; returns (seconds, ids, status)."""

@@ -8,6 +8,7 @@
 //   pick(weights, u)                                     src/common/sampling.cpp:9-19
 //   uniform(std::mt19937_64&)                            src/common/sampling.cpp:5-7
 //   haru::candidates(logits, haru::Sampling)             src/families/haru/sampler.cpp:18-61
+//   drama3::candidates(logits, drama3::Sampling)         src/families/drama3/sampler.cpp:30-60
 //
 // Status codes (identical to the product's per-row codes, include/speech_sampler_b200.h):
 //   0 ok; 1 Error(OutOfRange, "repetition_penalty"); 2 Error(OutOfRange, "temperature");
@@ -24,6 +25,7 @@
 #include <vector>
 
 #include "error.h"
+#include "drama3/sampler.h"
 #include "haru/sampler.h"
 #include "qwen3-tts/sampler.h"
 #include "sampling.h"
@@ -131,6 +133,27 @@ int ref_haru_candidates(const float * logits, int32_t n, float temperature, int3
         s.top_k = top_k;
         s.top_p = top_p;
         const Candidates c = haru::candidates(std::vector<float>(logits, logits + n), s);
+        *count = (int32_t) c.tokens.size();
+        for (int32_t i = 0; i < *count && i < cap; i++) {
+            tokens[i] = c.tokens[(size_t) i];
+            weights[i] = c.weights[(size_t) i];
+        }
+        return 0;
+    } catch (const std::exception & e) {
+        *count = 0;
+        return classify(e);
+    }
+}
+
+/** drama3::candidates(logits, {temperature, top_k, top_p}). */
+int ref_drama3_candidates(const float * logits, int32_t n, float temperature, int32_t top_k, float top_p,
+                          int32_t * tokens, double * weights, int32_t cap, int32_t * count) {
+    try {
+        drama3::Sampling s;
+        s.temperature = temperature;
+        s.top_k = top_k;
+        s.top_p = top_p;
+        const Candidates c = drama3::candidates(std::vector<float>(logits, logits + n), s);
         *count = (int32_t) c.tokens.size();
         for (int32_t i = 0; i < *count && i < cap; i++) {
             tokens[i] = c.tokens[(size_t) i];

@@ -361,3 +361,49 @@ int oracle_haru_candidates(const float * logits, int32_t n, float temperature, i
     free(s);
     return ORC_OK;
 }
+
+/*
+ * drama3::candidates(): drama3/sampler.cpp:30-60 — the logits divided by max(T, 1e-5) (:31-39, any
+ * non-finite logit is the device's error), k = min(max(top_k, 1), n), the k best by falling scaled
+ * logit with lowest-index ties (:40-45), the largest not finite -> temperature overflow (:46-47), the
+ * double sum of exp(s - top) over every token in index order (:48-49), then the tokens in order while
+ * the running share stays at most top_p, the first always (:50-58), each with weight exp(s - top).
+ * Returns a status (4 non-finite input, 2 temperature overflow); writes up to cap entries and *count.
+ */
+int oracle_drama3_candidates(const float * logits, int32_t n, float temperature, int32_t top_k, float top_p,
+                             int32_t * tokens, double * weights, int32_t cap, int32_t * count) {
+    *count = 0;
+    const float t = temperature > 1e-5f ? temperature : 1e-5f;
+    float * s = (float *) malloc(sizeof(float) * (size_t) n);
+    for (int32_t i = 0; i < n; i++) {
+        if (!isfinite(logits[i])) {
+            free(s);
+            return ORC_NON_FINITE_INPUT;
+        }
+        s[i] = logits[i] / t;
+    }
+    const int32_t k = top_k < 1 ? 1 : (top_k < n ? top_k : n);
+    orc_entry * e = (orc_entry *) malloc(sizeof(orc_entry) * (size_t) (k >= n / 4 ? n : k));
+    top_k_sorted(s, n, k, e);
+    const float top = e[0].v;
+    if (!isfinite(top)) {
+        free(e);
+        free(s);
+        return ORC_TEMPERATURE_OVERFLOW;
+    }
+    double sum = 0.0;
+    for (int32_t i = 0; i < n; i++) sum += exp((double) s[i] - top);
+    double cumulative = 0.0;
+    int32_t kept = 0;
+    for (int32_t r = 0; r < k; r++) {
+        const double p = exp((double) e[r].v - top);
+        cumulative += p / sum;
+        if (r > 0 && cumulative > top_p) break;
+        if (r < cap) tokens[r] = e[r].i, weights[r] = p;
+        kept++;
+    }
+    *count = kept;
+    free(e);
+    free(s);
+    return ORC_OK;
+}

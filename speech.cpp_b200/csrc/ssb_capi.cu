@@ -86,7 +86,7 @@ ssb_status ensure_nucleus_scratch(ssb_context * ctx, int grid, int64_t ld) {
 }
 
 struct Plan {
-    int kernel;  // 0 small, 1 stream (top-k / stream kernels), 2 nucleus (top-k above kStreamMaxK)
+    int kernel;  // 0 small, 1 stream (top-k / stream kernels), 2 nucleus (top-k above kStreamMaxK), 3 flavour
     int mode;    // stream: 0 greedy, 1 top-k
     int k_bound;
 };
@@ -99,7 +99,9 @@ ssb_status check_rows(const ssb_rows * r, bool device_side, Plan * plan) {
     if (r->ld < r->vocab) return fail(SSB_INVALID_ARGUMENT, "ld is smaller than vocab");
     if (r->dtype != SSB_F32 && r->dtype != SSB_BF16) return fail(SSB_INVALID_ARGUMENT, "dtype is neither SSB_F32 nor SSB_BF16");
     if (r->mask_kind < SSB_MASK_NONE || r->mask_kind > SSB_MASK_ALLOW) return fail(SSB_INVALID_ARGUMENT, "mask_kind is not an ssb_mask_kind");
-    if (r->reserved != 0 || r->params.reserved != 0) return fail(SSB_INVALID_ARGUMENT, "reserved fields must be 0");
+    if (r->reserved != 0) return fail(SSB_INVALID_ARGUMENT, "reserved fields must be 0");
+    if (r->params.flavor < SSB_FLAVOR_QWEN3_TTS || r->params.flavor > SSB_FLAVOR_DRAMA3)
+        return fail(SSB_INVALID_ARGUMENT, "params.flavor is not an ssb_flavor");
     if (r->rows == 0) return SSB_OK;
     if (!r->logits) return fail(SSB_INVALID_ARGUMENT, "logits is null");
     if (!r->ids || !r->status) return fail(SSB_INVALID_ARGUMENT, "ids and status are required");
@@ -112,7 +114,8 @@ ssb_status check_rows(const ssb_rows * r, bool device_side, Plan * plan) {
         if (r->history_ld < 0) return fail(SSB_INVALID_ARGUMENT, "history_ld is negative");
         if (r->history_ld > INT32_MAX / 2) return fail(SSB_OUT_OF_RANGE, "history_ld is too large");
     }
-    const bool all_greedy = !r->row_params && r->params.greedy;
+    const bool all_greedy = !r->row_params && (r->params.greedy || (r->params.flavor == SSB_FLAVOR_HARU &&
+                                                                    r->params.temperature <= 0.0f));
     if (!all_greedy && !r->u) return fail(SSB_INVALID_ARGUMENT, "u is required where a row draws (not greedy)");
     int kb;
     if (r->row_params) {
@@ -122,6 +125,22 @@ ssb_status check_rows(const ssb_rows * r, bool device_side, Plan * plan) {
         kb = r->params.greedy ? 1 : (r->params.top_k > 0 ? std::min(r->params.top_k, r->vocab) : r->vocab);
     }
     plan->k_bound = kb;
+    if (r->params.flavor != SSB_FLAVOR_QWEN3_TTS) {
+        // Haru's and Drama 3's candidate rules (ssb_flavor.cu), one CTA per row
+        const ssb_params & q = r->params;
+        const int keff = q.flavor == SSB_FLAVOR_HARU ? (q.top_k > 0 && q.top_k < r->vocab ? q.top_k : r->vocab)
+                                                     : std::min(std::max(q.top_k, 1), r->vocab);
+        const bool argmax = q.greedy || (q.flavor == SSB_FLAVOR_HARU && q.temperature <= 0.0f);
+        if (!r->row_params && !argmax && keff > ssb::kFlavorMaxK)
+            return fail(SSB_OUT_OF_RANGE, "the Haru and Drama 3 families keep at most 8192 candidates (top_k)");
+        if (!r->row_params) plan->k_bound = argmax ? 1 : keff;
+        plan->k_bound = std::min(plan->k_bound, ssb::kFlavorMaxK);
+        if (r->history && r->history_ld > SSB_MAX_STREAM_HISTORY)
+            return fail(SSB_OUT_OF_RANGE, "history_ld exceeds SSB_MAX_STREAM_HISTORY (8192)");
+        plan->kernel = 3;
+        plan->mode = 0;
+        return SSB_OK;
+    }
     if (r->vocab <= SSB_SMALL_VOCAB) {
         plan->kernel = 0;
         plan->mode = 0;
@@ -187,6 +206,21 @@ ssb_status run(ssb_context * ctx, const ssb_rows * r, const Debug * dbg, cudaStr
     if (plan.kernel == 0) {
         e = ssb::launch_small(a, bf16, debug, stream);
         if (e != cudaSuccess) return cuda_fail(e, "small-row kernel launch");
+        return ok();
+    }
+    if (plan.kernel == 3) {
+        ssb::FlavorArgs fa{};
+        fa.r = a;
+        fa.flavor = r->params.flavor;
+        fa.cap = ssb::next_pow2(std::max(plan.k_bound, 32));
+        fa.hist_slots = r->history ? ssb::next_pow2((int) std::max<int64_t>(4, 2 * r->history_ld)) : 0;
+        const int words = (int) div_up(r->vocab, 32);
+        fa.bit_words = r->history && words <= 16384 ? words : 0;  // the bitmap where it fits in 64 KB
+        if (ssb::flavor_smem_bytes(fa.cap, fa.bit_words, fa.hist_slots) > (size_t) ctx->max_smem) fa.bit_words = 0;
+        if (ssb::flavor_smem_bytes(fa.cap, fa.bit_words, fa.hist_slots) > (size_t) ctx->max_smem)
+            return fail(SSB_OUT_OF_RANGE, "the candidates and the history need more shared memory than the device has");
+        e = ssb::launch_flavor(fa, bf16, debug, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "flavour kernel launch");
         return ok();
     }
     if (plan.kernel == 2) {
@@ -414,7 +448,9 @@ ssb_status ssb_restrict_rows(ssb_context * ctx, const ssb_rows * r, float * out,
     if (r->ld < r->vocab) return fail(SSB_INVALID_ARGUMENT, "ld is smaller than vocab");
     if (r->dtype != SSB_F32 && r->dtype != SSB_BF16) return fail(SSB_INVALID_ARGUMENT, "dtype is neither SSB_F32 nor SSB_BF16");
     if (r->mask_kind < SSB_MASK_NONE || r->mask_kind > SSB_MASK_ALLOW) return fail(SSB_INVALID_ARGUMENT, "mask_kind is not an ssb_mask_kind");
-    if (r->reserved != 0 || r->params.reserved != 0) return fail(SSB_INVALID_ARGUMENT, "reserved fields must be 0");
+    if (r->reserved != 0) return fail(SSB_INVALID_ARGUMENT, "reserved fields must be 0");
+    if (r->params.flavor < SSB_FLAVOR_QWEN3_TTS || r->params.flavor > SSB_FLAVOR_DRAMA3)
+        return fail(SSB_INVALID_ARGUMENT, "params.flavor is not an ssb_flavor");
     if (!ctx) return fail(SSB_INVALID_ARGUMENT, "ctx is null");
     if (r->rows == 0) return ok();
     if (!r->logits) return fail(SSB_INVALID_ARGUMENT, "logits is null");

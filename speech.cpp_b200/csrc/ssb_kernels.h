@@ -91,6 +91,18 @@ int nucleus_threads();
 int nucleus_blocks_per_sm(bool bf16, size_t smem);
 cudaError_t launch_nucleus(const NucleusArgs & a, int grid, bool bf16, bool debug, cudaStream_t stream);
 
+// The Haru and Drama 3 candidate rules (ssb_flavor.cu): one CTA per row, at most kFlavorMaxK candidates.
+constexpr int kFlavorMaxK = 8192;
+struct FlavorArgs {
+    RowsArgs r;
+    int flavor;      // ssb_flavor of the call; a row of another family is INVALID_ROW
+    int cap;         // candidate slots (a power of two <= kFlavorMaxK); a drawing row with more is INVALID_ROW
+    int hist_slots;  // shared hash-table slots for the history (power of two >= 2 history_ld), or 0
+    int bit_words;   // words of the history-column bitmap (ceil(vocab / 32)), or 0 to look up the table
+};
+size_t flavor_smem_bytes(int cap, int bit_words, int hist_slots);
+cudaError_t launch_flavor(const FlavorArgs & a, bool bf16, bool debug, cudaStream_t stream);
+
 // The restricted logits alone (ssb_restrict.cu): every column widened to f32 with the mask applied,
 // then each row's history tokens penalized over it. `a` needs no ids, status or u.
 size_t restrict_smem_bytes(int hist_slots);

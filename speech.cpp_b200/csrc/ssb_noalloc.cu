@@ -108,7 +108,9 @@ extern "C" ssb_status ssb_sample_rows_noalloc(const ssb_rows * r, void * stream_
     if (r->ld < r->vocab) return fail(SSB_INVALID_ARGUMENT, "ld is smaller than vocab");
     if (r->dtype != SSB_F32 && r->dtype != SSB_BF16) return fail(SSB_INVALID_ARGUMENT, "dtype is neither SSB_F32 nor SSB_BF16");
     if (r->mask_kind < SSB_MASK_NONE || r->mask_kind > SSB_MASK_ALLOW) return fail(SSB_INVALID_ARGUMENT, "mask_kind is not an ssb_mask_kind");
-    if (r->reserved != 0 || r->params.reserved != 0) return fail(SSB_INVALID_ARGUMENT, "reserved fields must be 0");
+    if (r->reserved != 0) return fail(SSB_INVALID_ARGUMENT, "reserved fields must be 0");
+    if (r->params.flavor != SSB_FLAVOR_QWEN3_TTS)
+        return fail(SSB_OUT_OF_RANGE, "ssb_sample_rows_noalloc samples the Qwen3-TTS family; use ssb_sample_rows");
     if (r->rows == 0) {
         ssb::set_last_error("");
         return SSB_OK;

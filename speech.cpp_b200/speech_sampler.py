@@ -44,19 +44,24 @@ class Params(ctypes.Structure):
     _fields_ = [("greedy", ctypes.c_int32), ("temperature", ctypes.c_float), ("top_k", ctypes.c_int32),
                 ("top_p", ctypes.c_float), ("repetition_penalty", ctypes.c_float),
                 ("presence_penalty", ctypes.c_float), ("frequency_penalty", ctypes.c_float),
-                ("reserved", ctypes.c_int32)]
+                ("flavor", ctypes.c_int32)]
+
+
+FLAVOR_QWEN3_TTS, FLAVOR_HARU, FLAVOR_DRAMA3 = 0, 1, 2
 
 
 def params(greedy=False, temperature=1.0, top_k=0, top_p=1.0, repetition_penalty=1.0, presence_penalty=0.0,
-           frequency_penalty=0.0) -> Params:
-    """The reference's SamplingParams defaults (qwen3-tts/sampler.h:12-24) plus the extensions."""
+           frequency_penalty=0.0, flavor=FLAVOR_QWEN3_TTS) -> Params:
+    """The reference's SamplingParams defaults (qwen3-tts/sampler.h:12-24) plus the extensions; `flavor`
+    selects the candidate rules of the Haru (haru/sampler.cpp:18-61) or Drama 3
+    (drama3/sampler.cpp:18-59) families instead of Qwen3-TTS's."""
     return Params(int(bool(greedy)), temperature, int(top_k), top_p, repetition_penalty, presence_penalty,
-                  frequency_penalty, 0)
+                  frequency_penalty, int(flavor))
 
 
 PARAMS_DTYPE = np.dtype([("greedy", "<i4"), ("temperature", "<f4"), ("top_k", "<i4"), ("top_p", "<f4"),
                          ("repetition_penalty", "<f4"), ("presence_penalty", "<f4"),
-                         ("frequency_penalty", "<f4"), ("reserved", "<i4")])
+                         ("frequency_penalty", "<f4"), ("flavor", "<i4")])
 
 
 def params_array(plist) -> np.ndarray:
@@ -64,7 +69,7 @@ def params_array(plist) -> np.ndarray:
     a = np.zeros(len(plist), PARAMS_DTYPE)
     for i, p in enumerate(plist):
         a[i] = (p.greedy, p.temperature, p.top_k, p.top_p, p.repetition_penalty, p.presence_penalty,
-                p.frequency_penalty, 0)
+                p.frequency_penalty, p.flavor)
     return a
 
 

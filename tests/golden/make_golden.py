@@ -2,7 +2,8 @@
 sources into oracle/_ref/libref_sampler.so (oracle/Makefile). The reference ships no vectors for this
 path (its generators, reference/qwen3-tts/sampling_cases.py and reference/haru/sampling_cases.py, need
 model dumps), so the inputs here are seeded synthetic logits shaped like those cases, and the outputs
-are what the reference's sample(), candidates(), pick(), uniform() and haru::candidates() return.
+are what the reference's sample(), candidates(), pick(), uniform(), haru::candidates() and
+drama3::candidates() return.
 
 Run here, where the reference sources exist:   python tests/golden/make_golden.py
 The fixtures travel with the repository; the tests never need the reference at run time.
@@ -161,6 +162,45 @@ def haru_cases(ref: RefSampler) -> dict:
     return out
 
 
+# The settings of the reference's Drama 3 sampling cases (reference/drama3/sampling_cases.py:32-43): the
+# model card's, and cases around it; main-token rows span the end id and 4096 semantic ids (4097), the
+# residual codebooks' heads 4096 codes.
+DRAMA3_CASES = {
+    "card": (4097, 1.0, 30, 0.9),
+    "main-top-k-1": (4097, 1.0, 1, 0.9),
+    "codes-top-p-narrow": (4096, 1.0, 30, 0.1),
+    "codes-cold": (4096, 0.5, 30, 0.9),
+    "codes-hot": (4096, 1.5, 100, 1.0),
+    "main-every-token": (4097, 1.0, 4097, 1.0),
+}
+DRAMA3_ROWS = 4
+
+
+def drama3_cases(ref: RefSampler) -> dict:
+    """drama3::candidates() on seeded logits of each case's shape, and pick() of its weights with
+    seeded draws: tokens, weights (exp(s - top), not normalized), counts and the ids."""
+    out = {}
+    rng = np.random.default_rng(23)
+    for name, (n, t, k, p) in DRAMA3_CASES.items():
+        x = (rng.standard_normal((DRAMA3_ROWS, n), dtype=np.float32) * np.float32(rng.choice([1.5, 3.0, 6.0])))
+        u = rng.random(DRAMA3_ROWS)
+        cap = min(k, n)
+        toks = np.full((DRAMA3_ROWS, cap), -1, np.int32)
+        ws = np.zeros((DRAMA3_ROWS, cap))
+        ns = np.zeros(DRAMA3_ROWS, np.int32)
+        ids = np.zeros(DRAMA3_ROWS, np.int32)
+        for r in range(DRAMA3_ROWS):
+            st, tk, w = ref.drama3_candidates(x[r], t, k, p, cap=cap)
+            assert st == 0
+            ns[r] = len(tk)
+            toks[r, :len(tk)] = tk
+            ws[r, :len(tk)] = w
+            ids[r] = tk[ref.pick(w, u[r])]
+        out[name] = dict(logits=x, t=np.float32(t), k=np.int32(k), p=np.float32(p), u=u, tokens=toks, weights=ws,
+                         count=ns, ids=ids)
+    return out
+
+
 def main():
     build(ref=True)
     ref = RefSampler()
@@ -174,6 +214,9 @@ def main():
     flat = {"logits": h.pop("logits")}
     flat.update({f"{c}/{k}": v for c, d in h.items() for k, v in d.items()})
     np.savez_compressed(os.path.join(HERE, "haru_cases.npz"), **flat)
+    d = drama3_cases(ref)
+    np.savez_compressed(os.path.join(HERE, "drama3_cases.npz"),
+                        **{f"{c}/{k}": v for c, dd in d.items() for k, v in dd.items()})
     with open(os.path.join(HERE, "kat.json"), "w") as f:
         json.dump(kats(ref), f, indent=1)
     print("wrote", sorted(os.listdir(HERE)))

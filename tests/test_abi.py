@@ -60,6 +60,7 @@ def _rows(**kw):
     ("dtype", 7, ss.INVALID_ARGUMENT, "dtype"),
     ("mask_kind", 3, ss.INVALID_ARGUMENT, "mask_kind"),
     ("reserved", 1, ss.INVALID_ARGUMENT, "reserved"),
+    ("params", ss.params(flavor=3), ss.INVALID_ARGUMENT, "flavor"),
     ("logits", None, ss.INVALID_ARGUMENT, "logits"),
     ("ids", None, ss.INVALID_ARGUMENT, "ids"),
 ])

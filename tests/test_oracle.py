@@ -129,6 +129,39 @@ def test_haru_golden(oracle, case):
         assert np.array_equal(w, c["weights"][r, :len(tok)])
 
 
+@pytest.mark.parametrize("case", ["card", "main-top-k-1", "codes-top-p-narrow", "codes-cold", "codes-hot",
+                                  "main-every-token"])
+def test_drama3_golden(oracle, case):
+    """drama3::candidates() (drama3/sampler.cpp:30-60) as the compiled reference returned it: tokens and
+    weights bit for bit, and the id pick() draws from them."""
+    c = load_cases("drama3_cases.npz")[case]
+    for r in range(c["logits"].shape[0]):
+        st, tok, w = oracle.drama3_candidates(c["logits"][r], float(c["t"]), int(c["k"]), float(c["p"]))
+        n = int(c["count"][r])
+        assert st == 0 and len(tok) == n
+        assert np.array_equal(tok, c["tokens"][r, :n])
+        assert np.array_equal(w, c["weights"][r, :n])
+        assert tok[oracle.pick(w, c["u"][r])] == c["ids"][r]
+
+
+def test_drama3_refusals(oracle):
+    """Any non-finite logit is the device's error (status 4, drama3/sampler.cpp:35-37); a temperature
+    that takes the largest logit beyond a float overflows (2, :46-47); a temperature under 1e-5 divides
+    by 1e-5 (:31); top_k below 1 keeps one token (:40)."""
+    x = np.linspace(-3, 3, 300).astype(np.float32)
+    for bad in (np.nan, np.inf, -np.inf):
+        y = x.copy()
+        y[7] = bad
+        assert oracle.drama3_candidates(y, 1.0, 30, 0.9)[0] == 4
+    big = x * np.float32(1e34)
+    assert oracle.drama3_candidates(big, 1e-5, 30, 0.9)[0] == 2
+    a = oracle.drama3_candidates(x, 0.0, 30, 1.0)
+    b = oracle.drama3_candidates(x, 1e-5, 30, 1.0)
+    assert a[0] == 0 and np.array_equal(a[1], b[1]) and np.array_equal(a[2], b[2])
+    st, tok, w = oracle.drama3_candidates(x, 1.0, 0, 1.0)
+    assert st == 0 and list(tok) == [299] and list(w) == [1.0]
+
+
 # ---------------------------------------------------------------- extensions (parity unpinned)
 def test_presence_frequency_definition(oracle):
     """l -= frequency * count; l -= presence, after the repetition penalty, once per distinct id."""
@@ -195,3 +228,27 @@ def test_random_agreement_with_reference(oracle, ref):
         if (st1, id1) != (res["status"], res["id"]):
             mismatch.append((trial, st1, id1, res["status"], res["id"]))
     assert not mismatch
+
+
+def test_family_agreement_with_reference(oracle, ref):
+    """haru::candidates and drama3::candidates of the restatement against the compiled reference on random
+    rows (ties, -inf bans, top_k 0/1/beyond the vocabulary, top_p edges): identical statuses, tokens and
+    weights."""
+    rng = np.random.default_rng(77)
+    for trial in range(120):
+        n = int(rng.choice([1, 5, 300, 4096, 4097, 9000]))
+        x = (rng.standard_normal(n) * rng.choice([0.5, 2, 8])).astype(np.float32)
+        if rng.random() < 0.3:
+            x = np.round(x).astype(np.float32)  # ties
+        t = float(rng.choice([0.0, 1e-6, 0.5, 1.0, 1.7]))
+        k = int(rng.choice([0, 1, 30, 500, n, n + 3]))
+        p = float(rng.choice([0.0, 0.1, 0.9, 1.0]))
+        xh = x.copy()
+        if rng.random() < 0.3 and n > 2:
+            xh[rng.choice(n, max(1, n // 10), replace=False)] = -np.inf
+        for fam, xx in (("haru_candidates", xh), ("drama3_candidates", x)):
+            a = getattr(oracle, fam)(xx, t, k, p)
+            b = getattr(ref, fam)(xx, t, k, p)
+            assert a[0] == b[0], (trial, fam)
+            assert np.array_equal(a[1], b[1]), (trial, fam)
+            assert np.array_equal(a[2], b[2]), (trial, fam)
