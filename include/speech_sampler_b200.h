@@ -75,11 +75,13 @@ typedef enum ssb_mask_kind { SSB_MASK_NONE = 0, SSB_MASK_BAN = 1, SSB_MASK_ALLOW
  *   HARU       haru::candidates(), src/families/haru/sampler.cpp:18-61: float32 softmax, a temperature of
  *              0 or less (or greedy) draws the first maximum, top_k 0 or >= vocab keeps every token,
  *              top-p gives 0 weight to the tokens past it; NaN or +inf -> SSB_ROW_NON_FINITE_INPUT
- *   DRAMA3     drama3::candidates(), src/families/drama3/sampler.cpp:30-58: temperature at least 1e-5,
+ *   DRAMA3     drama3::candidates(), src/families/drama3/sampler.cpp:30-60: temperature at least 1e-5,
  *              top_k at least 1, the softmax over every token, the token that passes top_p dropped; any
- *              non-finite logit -> SSB_ROW_NON_FINITE_INPUT
- * HARU and DRAMA3 keep at most 4096 candidates: a larger effective top-k is refused (SSB_OUT_OF_RANGE;
- * SSB_ROW_INVALID_ROW for a row of row_params), and every row of a call must have the call's family.
+ *              non-finite stored logit -> SSB_ROW_NON_FINITE_INPUT; tokens the mask bans are no
+ *              candidates (SSB_ROW_NO_FINITE_LOGIT when none is left)
+ * HARU and DRAMA3 keep at most 8192 candidates: a larger effective top-k is refused (SSB_OUT_OF_RANGE;
+ * SSB_ROW_INVALID_ROW for a row of row_params beyond max_top_k), every row of a call must have the
+ * call's family (SSB_ROW_INVALID_ROW otherwise), and ssb_sample_rows_noalloc takes QWEN3_TTS only.
  */
 typedef enum ssb_flavor { SSB_FLAVOR_QWEN3_TTS = 0, SSB_FLAVOR_HARU = 1, SSB_FLAVOR_DRAMA3 = 2 } ssb_flavor;
 
@@ -199,9 +201,11 @@ SSB_API ssb_status ssb_sample_host(ssb_context *ctx, const ssb_rows *rows, void 
  * grow its footprint or synchronize the device on its decode path). No counterpart in the reference.
  * Pointers in `rows` are device pointers, as for ssb_sample_rows. The split-row scratch is a fixed
  * array of about 2.03 MiB inside the library, held by every GPU that loads it; the first call on each
- * device looks up its address (make it before any stream capture). Takes rows of more than
- * SSB_SMALL_VOCAB tokens, 16-byte aligned, with a top-k of at most 128 or greedy; anything else is
- * SSB_OUT_OF_RANGE. Calls share the array: calls that overlap on the GPU race and must not be made.
+ * device looks up its address, clears its per-row arrival counters once and waits for the device (make
+ * it before any stream capture); every launch leaves the counters at 0 again. Takes QWEN3_TTS rows of
+ * more than SSB_SMALL_VOCAB tokens, 16-byte aligned, with a top-k of at most 128 or greedy; anything
+ * else is SSB_OUT_OF_RANGE. Calls share the array: calls that overlap on the GPU race and must not be
+ * made.
  */
 SSB_API ssb_status ssb_sample_rows_noalloc(const ssb_rows *rows, void *stream);
 
