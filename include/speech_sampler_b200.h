@@ -179,6 +179,16 @@ SSB_API ssb_status ssb_candidates_rows(ssb_context *ctx, const ssb_rows *rows, i
                                        double *weights, int32_t *count, float *processed, void *stream);
 
 /*
+ * A device copy of a mask that many calls share (the talker's suppress mask of Generation::banned,
+ * src/families/qwen3-tts/sampler.cpp:62-67, built once per min_frames state instead of per step):
+ * copies `words` uint32 words (the ssb_rows.mask layout) from host memory, synchronously, into memory
+ * the context owns, and returns its device address in *device_words, valid until the context is
+ * destroyed. No counterpart in the reference, which builds a std::vector<bool> per call.
+ */
+SSB_API ssb_status ssb_context_mask(ssb_context *ctx, const uint32_t *host_words, int64_t words,
+                                    const uint32_t **device_words);
+
+/*
  * The restricted logits alone, the reference's restricted() (qwen3-tts/sampler.cpp:29-51) for a batch:
  * the repetition penalty (and the presence/frequency extension) over each row's distinct history ids,
  * then the mask (-inf where banned / not allowed), before the temperature, into out (f32, row r at

@@ -41,7 +41,7 @@ struct RefParams {
     float repetition_penalty;
     float presence_penalty;   // not a reference parameter: ignored here (see ref_time_rows)
     float frequency_penalty;  // not a reference parameter: ignored here (see ref_time_rows)
-    int32_t reserved;
+    int32_t flavor;           // not a reference parameter: ignored here
 };
 
 SamplingParams to_params(const RefParams * p) {

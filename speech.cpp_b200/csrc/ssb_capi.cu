@@ -7,6 +7,7 @@
 #include <cstring>
 #include <string>
 #include <thread>
+#include <vector>
 
 #include <cuda_runtime.h>
 
@@ -37,6 +38,8 @@ struct ssb_context {
     // occupancy of the top-k kernel per (warp-list width class, bf16)
     int occ_topk[3][2] = {};
     size_t occ_topk_smem[3][2] = {};  // the shared memory each was measured at
+    // device copies of caller masks (ssb_context_mask), freed with the context
+    std::vector<void *> masks;
 };
 
 namespace {
@@ -385,9 +388,29 @@ ssb_status ssb_context_destroy(ssb_context * ctx) {
     cudaFree(ctx->counters);
     cudaFree(ctx->stage);
     cudaFree(ctx->nuc_scratch);
+    for (void * m : ctx->masks) cudaFree(m);
     if (ctx->done) cudaEventDestroy(ctx->done);
     if (cur >= 0) cudaSetDevice(cur);
     delete ctx;
+    return ok();
+}
+
+ssb_status ssb_context_mask(ssb_context * ctx, const uint32_t * host_words, int64_t words, const uint32_t ** device_words) {
+    if (!ctx) return fail(SSB_INVALID_ARGUMENT, "ctx is null");
+    if (!host_words || !device_words) return fail(SSB_INVALID_ARGUMENT, "host_words and device_words are required");
+    if (words < 1 || words > SSB_MAX_VOCAB / 32) return fail(SSB_OUT_OF_RANGE, "words must be in [1, SSB_MAX_VOCAB / 32]");
+    ssb_status s = use_device(ctx);
+    if (s != SSB_OK) return s;
+    void * d = nullptr;
+    cudaError_t e = cudaMalloc(&d, (size_t) words * 4);
+    if (e != cudaSuccess) return cuda_fail(e, "mask copy");
+    e = cudaMemcpy(d, host_words, (size_t) words * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(d);
+        return cuda_fail(e, "mask copy");
+    }
+    ctx->masks.push_back(d);
+    *device_words = static_cast<const uint32_t *>(d);
     return ok();
 }
 
