@@ -14,6 +14,8 @@
  *   Qwen3Readback::Pick (device argmax, ASR greedy)     src/common/qwen3-decoder.h:80-92, .cpp:422-437
  *   Qwen3Decoder verify() argmax over [n, vocab]        src/common/qwen3-decoder.cpp:492-510
  *   host greedy max_element (ASR)                       src/families/qwen3-asr/decoder.cpp:108-113
+ *   haru::candidates, drama3::candidates (+ pick)       src/families/haru/sampler.cpp:18-61, drama3/sampler.cpp:30-60
+ *   haru::Dry::update / penalties, shape_logits         src/families/haru/sampler.cpp:82-124
  *   Error(Fault, message, input) refusals               src/common/error.h:8-38
  */
 #ifndef SPEECH_SAMPLER_B200_H
@@ -218,6 +220,62 @@ SSB_API ssb_status ssb_sample_host(ssb_context *ctx, const ssb_rows *rows, void 
  * made.
  */
 SSB_API ssb_status ssb_sample_rows_noalloc(const ssb_rows *rows, void *stream);
+
+/* ---------------------------------------------------------------- Haru's logit shaping and DRY */
+
+/* DryConfig (haru/sampler.h:37-40, read by file_dry, haru/sampler.cpp:63-73). */
+typedef struct ssb_dry_config {
+    double multiplier;
+    double base;
+    double max_penalty;
+    int32_t allowed_length;
+    int32_t lookback;
+    int32_t max_match_length;
+    int32_t reserved; /* must be 0 */
+} ssb_dry_config;
+
+/* The DRY state of `streams` text streams on the device (haru::Dry, haru/sampler.h:49-69): each stream's
+ * last lookback + max_match_length + 1 drawn tokens but the exempt ones, and its penalties. */
+typedef struct ssb_dry ssb_dry;
+
+#define SSB_DRY_MAX_WINDOW 8192 /* lookback + max_match_length + 1 limit */
+#define SSB_DRY_MAX_EXEMPT 64
+
+/* Creates the state of `streams` empty streams on the context's device; `exempt` (host, n_exempt ids)
+ * are the tokens Dry(config, exempt) leaves out (haru/dialogue.cpp:128 passes PAD, EOP and EOS). */
+SSB_API ssb_status ssb_dry_create(ssb_context *ctx, const ssb_dry_config *config, int32_t streams,
+                                  const int32_t *exempt, int32_t n_exempt, ssb_dry **out);
+SSB_API ssb_status ssb_dry_destroy(ssb_dry *dry);
+
+/* Dry::update(token) (haru/sampler.cpp:86-110) for every stream: tokens[s] (device, [streams]) is
+ * stream s's drawn token; a negative token leaves the stream as it is. Asynchronous on `stream`: the
+ * tokens may be the ids an ssb_sample_rows call wrote just before on the same stream. */
+SSB_API ssb_status ssb_dry_update(ssb_dry *dry, const int32_t *tokens, void *stream);
+
+/* Dry::penalties() of stream `s` (by rising token), copied to host memory after the work queued on
+ * `stream`: up to `cap` entries and the full count. */
+SSB_API ssb_status ssb_dry_penalties(const ssb_dry *dry, int32_t s, int32_t *tokens, double *penalties, int32_t cap,
+                                     int32_t *count, void *stream);
+
+/* shape_logits() (haru/sampler.cpp:116-124) for rows of f32 logits on the device, in place: row r is
+ * stream r of `dry` (or no DRY penalty when dry is null); each DRY penalty rounded to float is
+ * subtracted from its token's logit, PAD's and EOP's logits are replaced by silent[r * silent_ld + 0]
+ * and [+ 1] (plus eop_bias where it is not 0), and where must_speak[r] is nonzero PAD, EOP and EOS are
+ * set to -inf. Rows then go to ssb_sample_rows with params.flavor = SSB_FLAVOR_HARU. */
+typedef struct ssb_haru_shape {
+    float *logits;             /* [rows, ld] f32, device, modified in place */
+    int64_t ld;
+    int32_t rows;              /* at most the DRY state's streams when dry is given */
+    int32_t vocab;
+    const float *silent;       /* [rows, silent_ld] device: PAD's and EOP's logits of the silent head */
+    int64_t silent_ld;         /* >= 2 */
+    int32_t pad, eop, eos;     /* haru::TextIds (haru/sampler.h:43-45), each in [0, vocab) */
+    float eop_bias;
+    const int32_t *must_speak; /* [rows] device, or null (no row must speak) */
+} ssb_haru_shape;
+
+SSB_API ssb_status ssb_haru_shape_rows(ssb_context *ctx, const ssb_haru_shape *shape, const ssb_dry *dry,
+                                       void *stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

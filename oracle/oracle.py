@@ -89,6 +89,12 @@ class Oracle:
         lib.oracle_pick.argtypes = [ctypes.POINTER(ctypes.c_double), ctypes.c_int32, ctypes.c_double]
         lib.oracle_uniform.restype = None
         lib.oracle_uniform.argtypes = [ctypes.c_uint64, ctypes.c_int64, ctypes.POINTER(ctypes.c_double)]
+        _bind_dry(lib, "oracle_dry_run")
+        lib.oracle_haru_shape.restype = None
+        lib.oracle_haru_shape.argtypes = [ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_int32),
+                                          ctypes.POINTER(ctypes.c_double), ctypes.c_int32,
+                                          ctypes.POINTER(ctypes.c_float), ctypes.c_int32, ctypes.c_int32,
+                                          ctypes.c_int32, ctypes.c_float, ctypes.c_int32]
         for name in ("oracle_haru_candidates", "oracle_drama3_candidates"):
             f = getattr(lib, name)
             f.restype = ctypes.c_int
@@ -149,6 +155,21 @@ class Oracle:
         self.lib.oracle_uniform(seed, n, _p(out, ctypes.c_double))
         return out
 
+    def dry_run(self, cfg, exempt, tokens, cap=256):
+        """Dry::update over `tokens` (haru/sampler.cpp:86-110): penalties after each step
+        (tokens [n, cap], values [n, cap], counts [n])."""
+        return _dry_run(self.lib.oracle_dry_run, cfg, exempt, tokens, cap)
+
+    def haru_shape(self, logits, pen_tokens, pen_values, silent, pad, eop, eos, eop_bias, must_speak):
+        """shape_logits (haru/sampler.cpp:116-124) of one f32 row (a copy is returned)."""
+        x = np.array(logits, np.float32)
+        pt = np.ascontiguousarray(pen_tokens, np.int32)
+        pv = np.ascontiguousarray(pen_values, np.float64)
+        sil = np.ascontiguousarray(silent, np.float32)
+        self.lib.oracle_haru_shape(_p(x, ctypes.c_float), _p(pt, ctypes.c_int32), _p(pv, ctypes.c_double), len(pt),
+                                   _p(sil, ctypes.c_float), pad, eop, eos, eop_bias, int(must_speak))
+        return x
+
     def _family(self, f, logits, temperature, top_k, top_p, cap):
         x = np.ascontiguousarray(logits, dtype=np.float32)
         cap = len(x) if cap is None else cap
@@ -167,6 +188,33 @@ class Oracle:
     def drama3_candidates(self, logits, temperature, top_k, top_p, cap=None):
         """drama3::candidates (drama3/sampler.cpp:30-60): (status, tokens, weights)."""
         return self._family(self.lib.oracle_drama3_candidates, logits, temperature, top_k, top_p, cap)
+
+
+class DryConfig(ctypes.Structure):
+    """ssb_dry_config / haru::DryConfig (haru/sampler.h:37-40)."""
+    _fields_ = [("multiplier", ctypes.c_double), ("base", ctypes.c_double), ("max_penalty", ctypes.c_double),
+                ("allowed_length", ctypes.c_int32), ("lookback", ctypes.c_int32),
+                ("max_match_length", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+
+
+def _dry_run(f, cfg, exempt, tokens, cap):
+    ex = np.ascontiguousarray(exempt, np.int32)
+    t = np.ascontiguousarray(tokens, np.int32)
+    n = len(t)
+    pt = np.full((n, cap), -1, np.int32)
+    pv = np.zeros((n, cap))
+    cnt = np.zeros(n, np.int32)
+    f(ctypes.byref(cfg), _p(ex, ctypes.c_int32), len(ex), _p(t, ctypes.c_int32), n, _p(pt, ctypes.c_int32),
+      _p(pv, ctypes.c_double), cap, _p(cnt, ctypes.c_int32))
+    return pt, pv, cnt
+
+
+def _bind_dry(lib, run_name):
+    f = getattr(lib, run_name)
+    f.restype = None
+    f.argtypes = [ctypes.POINTER(DryConfig), ctypes.POINTER(ctypes.c_int32), ctypes.c_int32,
+                  ctypes.POINTER(ctypes.c_int32), ctypes.c_int64, ctypes.POINTER(ctypes.c_int32),
+                  ctypes.POINTER(ctypes.c_double), ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)]
 
 
 class RefSampler:
@@ -189,6 +237,11 @@ class RefSampler:
         lib.ref_pick.argtypes = [f64p, ctypes.c_int32, ctypes.c_double]
         lib.ref_uniform.restype = None
         lib.ref_uniform.argtypes = [ctypes.c_uint64, ctypes.c_int64, f64p]
+        _bind_dry(lib, "ref_dry_run")
+        lib.ref_haru_shape.restype = None
+        lib.ref_haru_shape.argtypes = [f32p, ctypes.c_int32, ctypes.POINTER(DryConfig), i32p, ctypes.c_int32, i32p,
+                                       ctypes.c_int64, f32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                       ctypes.c_float, ctypes.c_int32]
         for name in ("ref_haru_candidates", "ref_drama3_candidates"):
             f = getattr(lib, name)
             f.restype = ctypes.c_int
@@ -244,6 +297,20 @@ class RefSampler:
 
     def drama3_candidates(self, logits, temperature, top_k, top_p, cap=None):
         return Oracle._family(self, self.lib.ref_drama3_candidates, logits, temperature, top_k, top_p, cap)
+
+    def dry_run(self, cfg, exempt, tokens, cap=256):
+        return _dry_run(self.lib.ref_dry_run, cfg, exempt, tokens, cap)
+
+    def haru_shape(self, logits, cfg, exempt, tokens, silent, pad, eop, eos, eop_bias, must_speak):
+        """shape_logits with the reference's own Dry after `tokens` (a copy is returned)."""
+        x = np.array(logits, np.float32)
+        ex = np.ascontiguousarray(exempt, np.int32)
+        t = np.ascontiguousarray(tokens, np.int32)
+        sil = np.ascontiguousarray(silent, np.float32)
+        self.lib.ref_haru_shape(_p(x, ctypes.c_float), len(x), ctypes.byref(cfg), _p(ex, ctypes.c_int32), len(ex),
+                                _p(t, ctypes.c_int32), len(t), _p(sil, ctypes.c_float), pad, eop, eos, eop_bias,
+                                int(must_speak))
+        return x
 
     def time_rows(self, logits_f32, p: Params, history=None, hlens=None, banned=None, u=None, threads=1):
         """sample() over every row with `threads` workers; returns (seconds, ids, status)."""

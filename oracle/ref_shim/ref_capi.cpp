@@ -9,6 +9,7 @@
 //   uniform(std::mt19937_64&)                            src/common/sampling.cpp:5-7
 //   haru::candidates(logits, haru::Sampling)             src/families/haru/sampler.cpp:18-61
 //   drama3::candidates(logits, drama3::Sampling)         src/families/drama3/sampler.cpp:30-60
+//   haru::Dry::update / penalties, shape_logits          src/families/haru/sampler.cpp:82-124
 //
 // Status codes (identical to the product's per-row codes, include/speech_sampler_b200.h):
 //   0 ok; 1 Error(OutOfRange, "repetition_penalty"); 2 Error(OutOfRange, "temperature");
@@ -164,6 +165,53 @@ int ref_drama3_candidates(const float * logits, int32_t n, float temperature, in
         *count = 0;
         return classify(e);
     }
+}
+
+/** Same layout as ssb_dry_config. */
+struct RefDryConfig {
+    double multiplier, base, max_penalty;
+    int32_t allowed_length, lookback, max_match_length, reserved;
+};
+
+static haru::Dry make_dry(const RefDryConfig * c, const int32_t * exempt, int32_t n_exempt) {
+    haru::DryConfig d;
+    d.multiplier = c->multiplier;
+    d.base = c->base;
+    d.max_penalty = c->max_penalty;
+    d.allowed_length = c->allowed_length;
+    d.lookback = c->lookback;
+    d.max_match_length = c->max_match_length;
+    return haru::Dry(d, std::vector<int32_t>(exempt, exempt + n_exempt));
+}
+
+/** haru::Dry::update over `tokens`, the penalties() after each: [n_tokens, cap] and counts [n_tokens]. */
+void ref_dry_run(const RefDryConfig * c, const int32_t * exempt, int32_t n_exempt, const int32_t * tokens,
+                 int64_t n_tokens, int32_t * pen_tokens, double * pen_values, int32_t cap, int32_t * counts) {
+    haru::Dry dry = make_dry(c, exempt, n_exempt);
+    for (int64_t s = 0; s < n_tokens; s++) {
+        dry.update(tokens[s]);
+        const auto & p = dry.penalties();
+        counts[s] = (int32_t) p.size();
+        for (size_t i = 0; i < p.size() && (int32_t) i < cap; i++) {
+            pen_tokens[s * cap + (int64_t) i] = p[i].first;
+            pen_values[s * cap + (int64_t) i] = p[i].second;
+        }
+    }
+}
+
+/** shape_logits(logits, dry after `tokens`, silent, {pad, eop, eos}, eop_bias, must_speak) in place. */
+void ref_haru_shape(float * logits, int32_t n, const RefDryConfig * c, const int32_t * exempt, int32_t n_exempt,
+                    const int32_t * tokens, int64_t n_tokens, const float * silent, int32_t pad, int32_t eop,
+                    int32_t eos, float eop_bias, int32_t must_speak) {
+    haru::Dry dry = make_dry(c, exempt, n_exempt);
+    for (int64_t s = 0; s < n_tokens; s++) dry.update(tokens[s]);
+    std::vector<float> l(logits, logits + n);
+    haru::TextIds ids;
+    ids.pad = pad;
+    ids.eop = eop;
+    ids.eos = eos;
+    haru::shape_logits(l, dry, silent, ids, eop_bias, must_speak != 0);
+    std::copy(l.begin(), l.end(), logits);
 }
 
 /**

@@ -407,3 +407,96 @@ int oracle_drama3_candidates(const float * logits, int32_t n, float temperature,
     free(s);
     return ORC_OK;
 }
+
+/*
+ * haru::Dry (haru/sampler.cpp:82-114). The settings have ssb_dry_config's layout. oracle_dry_run feeds
+ * `tokens` to Dry::update one after another and writes the penalties after each (by rising token, up to
+ * cap per step: pen_tokens/pen_values [n_tokens, cap], counts [n_tokens]). An exempt token leaves the
+ * state, penalties included, as it was (:87).
+ */
+typedef struct {
+    double multiplier, base, max_penalty;
+    int32_t allowed_length, lookback, max_match_length, reserved;
+} orc_dry_config;
+
+typedef struct {
+    int32_t token, length;
+} orc_match;
+
+static int orc_match_cmp(const void * a, const void * b) {
+    const orc_match * x = (const orc_match *) a, * y = (const orc_match *) b;
+    if (x->token != y->token) return x->token < y->token ? -1 : 1;
+    return (x->length > y->length) - (x->length < y->length);
+}
+
+static int orc_in(const int32_t * ids, int32_t n, int32_t t) {
+    for (int32_t i = 0; i < n; i++)
+        if (ids[i] == t) return 1;
+    return 0;
+}
+
+void oracle_dry_run(const orc_dry_config * c, const int32_t * exempt, int32_t n_exempt, const int32_t * tokens,
+                    int64_t n_tokens, int32_t * pen_tokens, double * pen_values, int32_t cap, int32_t * counts) {
+    const int64_t size = (int64_t) c->lookback + c->max_match_length + 1;
+    int32_t * h = (int32_t *) malloc(sizeof(int32_t) * (size_t) (size + 1));
+    orc_match * m = (orc_match *) malloc(sizeof(orc_match) * (size_t) (size + 1));
+    int32_t * pt = (int32_t *) malloc(sizeof(int32_t) * (size_t) (size + 1));
+    double * pv = (double *) malloc(sizeof(double) * (size_t) (size + 1));
+    int64_t hn = 0;
+    int32_t np = 0;
+    for (int64_t s = 0; s < n_tokens; s++) {
+        const int32_t token = tokens[s];
+        if (!orc_in(exempt, n_exempt, token)) {
+            h[hn++] = token;
+            if (hn > size) {
+                memmove(h, h + (hn - size), sizeof(int32_t) * (size_t) size);
+                hn = size;
+            }
+            np = 0;
+            const int32_t need = c->allowed_length > 1 ? c->allowed_length : 1;
+            if (hn >= need) {
+                int32_t nm = 0;
+                const int32_t last = h[hn - 1];
+                const int64_t jlo = hn - 1 - c->lookback > 0 ? hn - 1 - c->lookback : 0;
+                for (int64_t j = hn - 2; j >= jlo; j--) {
+                    if (h[j] != last) continue;
+                    int32_t length = 1;
+                    while (length < c->max_match_length && j - length >= 0 && h[j - length] == h[hn - 1 - length]) length++;
+                    if (length >= c->allowed_length) m[nm].token = h[j + 1], m[nm].length = length, nm++;
+                }
+                qsort(m, (size_t) nm, sizeof(orc_match), orc_match_cmp);
+                for (int32_t i = 0; i < nm; i++) {
+                    if (i + 1 < nm && m[i + 1].token == m[i].token) continue;  /* the longest is last */
+                    if (orc_in(exempt, n_exempt, m[i].token)) continue;
+                    const double pen = c->multiplier * pow(c->base, (double) (m[i].length - c->allowed_length));
+                    pt[np] = m[i].token;
+                    pv[np] = pen < c->max_penalty ? pen : c->max_penalty;  /* std::min(max_penalty, pen) */
+                    np++;
+                }
+            }
+        }
+        counts[s] = np;
+        for (int32_t i = 0; i < np && i < cap; i++) {
+            pen_tokens[s * cap + i] = pt[i];
+            pen_values[s * cap + i] = pv[i];
+        }
+    }
+    free(pv);
+    free(pt);
+    free(m);
+    free(h);
+}
+
+/*
+ * shape_logits() (haru/sampler.cpp:116-124) on one f32 row in place: each penalty rounded to float
+ * subtracted from its token's logit, PAD's and EOP's logits replaced by silent[0] and silent[1], the EOP
+ * bias added where it is not 0, and PAD, EOP and EOS to -inf where the row must speak.
+ */
+void oracle_haru_shape(float * logits, const int32_t * pen_tokens, const double * pen_values, int32_t n_pen,
+                       const float * silent, int32_t pad, int32_t eop, int32_t eos, float eop_bias, int32_t must_speak) {
+    for (int32_t i = 0; i < n_pen; i++) logits[pen_tokens[i]] -= (float) pen_values[i];
+    logits[pad] = silent[0];
+    logits[eop] = silent[1];
+    if (eop_bias != 0.0f) logits[eop] += eop_bias;
+    if (must_speak) logits[pad] = logits[eop] = logits[eos] = -INFINITY;
+}

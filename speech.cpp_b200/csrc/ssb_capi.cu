@@ -42,6 +42,14 @@ struct ssb_context {
     std::vector<void *> masks;
 };
 
+// The DRY state of Haru's text streams (one device allocation).
+struct ssb_dry {
+    int device = 0;
+    int max_smem = 0;
+    void * block = nullptr;
+    ssb::DryArgs a{};
+};
+
 namespace {
 
 thread_local std::string g_error;
@@ -560,6 +568,148 @@ ssb_status ssb_sample_host(ssb_context * ctx, const ssb_rows * rows, void * stre
     if (e != cudaSuccess) return cuda_fail(e, "copying the ids back");
     s = wait_stream(ctx, stream, 60.0);
     if (s != SSB_OK) return s;
+    return ok();
+}
+
+// ---------------------------------------------------------------- Haru: DRY and logit shaping
+
+ssb_status ssb_dry_create(ssb_context * ctx, const ssb_dry_config * config, int32_t streams, const int32_t * exempt,
+                          int32_t n_exempt, ssb_dry ** out) {
+    if (!ctx || !config || !out) return fail(SSB_INVALID_ARGUMENT, "ctx, config and out are required");
+    *out = nullptr;
+    if (config->reserved != 0) return fail(SSB_INVALID_ARGUMENT, "reserved fields must be 0");
+    if (streams < 1) return fail(SSB_INVALID_ARGUMENT, "streams must be at least 1");
+    if (config->lookback < 0 || config->max_match_length < 0)
+        return fail(SSB_INVALID_ARGUMENT, "lookback and max_match_length must not be negative");
+    if ((int64_t) config->lookback + config->max_match_length + 1 > SSB_DRY_MAX_WINDOW)
+        return fail(SSB_OUT_OF_RANGE, "lookback + max_match_length + 1 exceeds SSB_DRY_MAX_WINDOW (8192)");
+    if (n_exempt < 0 || n_exempt > SSB_DRY_MAX_EXEMPT || (n_exempt > 0 && !exempt))
+        return fail(SSB_INVALID_ARGUMENT, "exempt must hold n_exempt ids, at most SSB_DRY_MAX_EXEMPT (64)");
+    ssb_status st = use_device(ctx);
+    if (st != SSB_OK) return st;
+    ssb_dry * d = new ssb_dry();
+    d->device = ctx->device;
+    d->max_smem = ctx->max_smem;
+    ssb::DryArgs & a = d->a;
+    a.cfg = ssb::DryConfigD{config->multiplier, config->base, config->max_penalty, config->allowed_length,
+                            config->lookback, config->max_match_length};
+    a.streams = streams;
+    a.window = config->lookback + config->max_match_length + 1;
+    a.rec_slots = ssb::next_pow2(a.window);
+    a.pen_cap = std::max(1, config->lookback);
+    a.n_exempt = n_exempt;
+    const size_t n = (size_t) streams;
+    const size_t bytes = n * a.window * 4 + 3 * n * 4 + n * a.pen_cap * 4 + n * a.pen_cap * 8 + SSB_DRY_MAX_EXEMPT * 4 + 64;
+    cudaError_t e = cudaMalloc(&d->block, bytes);
+    if (e == cudaSuccess) e = cudaMemset(d->block, 0, bytes);
+    if (e != cudaSuccess) {
+        cudaFree(d->block);
+        delete d;
+        return cuda_fail(e, "DRY state");
+    }
+    unsigned char * p = static_cast<unsigned char *>(d->block);
+    a.pen_val = reinterpret_cast<double *>(p);  // 8-byte aligned first
+    p += n * a.pen_cap * 8;
+    a.hist = reinterpret_cast<int32_t *>(p);
+    p += n * a.window * 4;
+    a.head = reinterpret_cast<int32_t *>(p);
+    p += n * 4;
+    a.count = reinterpret_cast<int32_t *>(p);
+    p += n * 4;
+    a.pen_n = reinterpret_cast<int32_t *>(p);
+    p += n * 4;
+    a.pen_tok = reinterpret_cast<int32_t *>(p);
+    p += n * a.pen_cap * 4;
+    int32_t * ex = reinterpret_cast<int32_t *>(p);
+    if (n_exempt > 0) {
+        e = cudaMemcpy(ex, exempt, (size_t) n_exempt * 4, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            cudaFree(d->block);
+            delete d;
+            return cuda_fail(e, "DRY exempt ids");
+        }
+    }
+    a.exempt = ex;
+    if (ssb::dry_smem_bytes(a.window) > (size_t) ctx->max_smem) {
+        cudaFree(d->block);
+        delete d;
+        return fail(SSB_OUT_OF_RANGE, "the DRY window needs more shared memory than the device has");
+    }
+    *out = d;
+    return ok();
+}
+
+ssb_status ssb_dry_destroy(ssb_dry * d) {
+    if (!d) return ok();
+    int cur = -1;
+    cudaGetDevice(&cur);
+    cudaSetDevice(d->device);
+    cudaFree(d->block);
+    if (cur >= 0) cudaSetDevice(cur);
+    delete d;
+    return ok();
+}
+
+ssb_status ssb_dry_update(ssb_dry * d, const int32_t * tokens, void * stream_ptr) {
+    if (!d || !tokens) return fail(SSB_INVALID_ARGUMENT, "dry and tokens are required");
+    cudaError_t e = cudaSetDevice(d->device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    e = ssb::launch_dry_update(d->a, tokens, static_cast<cudaStream_t>(stream_ptr));
+    if (e != cudaSuccess) return cuda_fail(e, "DRY update launch");
+    return ok();
+}
+
+ssb_status ssb_dry_penalties(const ssb_dry * d, int32_t s, int32_t * tokens, double * penalties, int32_t cap,
+                             int32_t * count, void * stream_ptr) {
+    if (!d || !count || (cap > 0 && (!tokens || !penalties)))
+        return fail(SSB_INVALID_ARGUMENT, "dry, count and (for cap > 0) tokens and penalties are required");
+    if (s < 0 || s >= d->a.streams) return fail(SSB_INVALID_ARGUMENT, "s is not a stream of this state");
+    cudaError_t e = cudaSetDevice(d->device);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream_ptr));
+    int32_t n = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&n, d->a.pen_n + s, 4, cudaMemcpyDeviceToHost);
+    const int32_t c = std::min(n, std::max(cap, 0));
+    if (e == cudaSuccess && c > 0)
+        e = cudaMemcpy(tokens, d->a.pen_tok + (int64_t) s * d->a.pen_cap, (size_t) c * 4, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && c > 0)
+        e = cudaMemcpy(penalties, d->a.pen_val + (int64_t) s * d->a.pen_cap, (size_t) c * 8, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "reading the DRY penalties");
+    *count = n;
+    return ok();
+}
+
+ssb_status ssb_haru_shape_rows(ssb_context * ctx, const ssb_haru_shape * h, const ssb_dry * d, void * stream_ptr) {
+    if (!ctx || !h) return fail(SSB_INVALID_ARGUMENT, "ctx and shape are required");
+    if (h->rows < 0 || h->vocab < 1) return fail(SSB_INVALID_ARGUMENT, "rows is negative or vocab below 1");
+    if (h->rows == 0) return ok();
+    if (!h->logits || !h->silent) return fail(SSB_INVALID_ARGUMENT, "logits and silent are required");
+    if (h->ld < h->vocab || h->silent_ld < 2) return fail(SSB_INVALID_ARGUMENT, "ld is below vocab or silent_ld below 2");
+    for (int32_t id : {h->pad, h->eop, h->eos})
+        if (id < 0 || id >= h->vocab) return fail(SSB_INVALID_ARGUMENT, "pad, eop and eos must lie in [0, vocab)");
+    if (d && (d->device != ctx->device || h->rows > d->a.streams))
+        return fail(SSB_INVALID_ARGUMENT, "the DRY state has fewer streams than rows, or lives on another device");
+    ssb_status st = use_device(ctx);
+    if (st != SSB_OK) return st;
+    ssb::ShapeArgs a{};
+    a.logits = h->logits;
+    a.ld = h->ld;
+    a.rows = h->rows;
+    a.vocab = h->vocab;
+    a.silent = h->silent;
+    a.silent_ld = h->silent_ld;
+    a.pad = h->pad;
+    a.eop = h->eop;
+    a.eos = h->eos;
+    a.eop_bias = h->eop_bias;
+    a.must_speak = h->must_speak;
+    if (d) {
+        a.pen_n = d->a.pen_n;
+        a.pen_tok = d->a.pen_tok;
+        a.pen_val = d->a.pen_val;
+        a.pen_cap = d->a.pen_cap;
+    }
+    const cudaError_t e = ssb::launch_haru_shape(a, static_cast<cudaStream_t>(stream_ptr));
+    if (e != cudaSuccess) return cuda_fail(e, "Haru shaping launch");
     return ok();
 }
 

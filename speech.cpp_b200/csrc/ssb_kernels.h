@@ -103,6 +103,44 @@ struct FlavorArgs {
 size_t flavor_smem_bytes(int cap, int bit_words, int hist_slots);
 cudaError_t launch_flavor(const FlavorArgs & a, bool bf16, bool debug, cudaStream_t stream);
 
+// Haru's DRY state update and logit shaping (ssb_haru.cu).
+struct DryConfigD {
+    double multiplier, base, max_penalty;
+    int allowed_length, lookback, max_match_length;
+};
+struct DryArgs {
+    DryConfigD cfg;
+    int streams;
+    int window;     // ring capacity: lookback + max_match_length + 1
+    int rec_slots;  // next_pow2(window): shared records of one update
+    int32_t * hist;   // [streams, window] ring of drawn tokens
+    int32_t * head;   // [streams] slot of the oldest
+    int32_t * count;  // [streams] tokens held
+    int32_t * pen_tok;  // [streams, pen_cap] penalties by rising token
+    double * pen_val;   // [streams, pen_cap]
+    int32_t * pen_n;    // [streams]
+    int pen_cap;        // max(1, lookback): at most one proposal per earlier position
+    const int32_t * exempt;  // [n_exempt] device
+    int n_exempt;
+};
+struct ShapeArgs {
+    float * logits;
+    int64_t ld;
+    int rows, vocab;
+    const float * silent;
+    int64_t silent_ld;
+    int pad, eop, eos;
+    float eop_bias;
+    const int32_t * must_speak;
+    const int32_t * pen_n;  // null: no DRY
+    const int32_t * pen_tok;
+    const double * pen_val;
+    int pen_cap;
+};
+size_t dry_smem_bytes(int window);
+cudaError_t launch_dry_update(const DryArgs & a, const int32_t * tokens, cudaStream_t stream);
+cudaError_t launch_haru_shape(const ShapeArgs & a, cudaStream_t stream);
+
 // The restricted logits alone (ssb_restrict.cu): every column widened to f32 with the mask applied,
 // then each row's history tokens penalized over it. `a` needs no ids, status or u.
 size_t restrict_smem_bytes(int hist_slots);

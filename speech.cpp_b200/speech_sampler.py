@@ -82,6 +82,21 @@ class Rows(ctypes.Structure):
                 ("u", ctypes.c_void_p), ("ids", ctypes.c_void_p), ("status", ctypes.c_void_p)]
 
 
+class DryConfig(ctypes.Structure):
+    """ssb_dry_config: haru::DryConfig (haru/sampler.h:37-40)."""
+    _fields_ = [("multiplier", ctypes.c_double), ("base", ctypes.c_double), ("max_penalty", ctypes.c_double),
+                ("allowed_length", ctypes.c_int32), ("lookback", ctypes.c_int32),
+                ("max_match_length", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+
+
+class HaruShape(ctypes.Structure):
+    """ssb_haru_shape: shape_logits()'s inputs for rows on the device (haru/sampler.cpp:116-124)."""
+    _fields_ = [("logits", ctypes.c_void_p), ("ld", ctypes.c_int64), ("rows", ctypes.c_int32),
+                ("vocab", ctypes.c_int32), ("silent", ctypes.c_void_p), ("silent_ld", ctypes.c_int64),
+                ("pad", ctypes.c_int32), ("eop", ctypes.c_int32), ("eos", ctypes.c_int32),
+                ("eop_bias", ctypes.c_float), ("must_speak", ctypes.c_void_p)]
+
+
 def header_symbols(path: str = HEADER):
     """Every function the C header declares (SSB_API ... name(...))."""
     text = open(path).read()
@@ -116,6 +131,18 @@ def load_library(path: str = LIB_PATH):
     lib.ssb_sample_host.argtypes = [vp, ctypes.POINTER(Rows), vp]
     lib.ssb_restrict_rows.restype = ctypes.c_int
     lib.ssb_restrict_rows.argtypes = [vp, ctypes.POINTER(Rows), vp, ctypes.c_int64, vp]
+    lib.ssb_context_mask.restype = ctypes.c_int
+    lib.ssb_context_mask.argtypes = [vp, vp, ctypes.c_int64, ctypes.POINTER(vp)]
+    lib.ssb_dry_create.restype = ctypes.c_int
+    lib.ssb_dry_create.argtypes = [vp, ctypes.POINTER(DryConfig), i32, vp, i32, ctypes.POINTER(vp)]
+    lib.ssb_dry_destroy.restype = ctypes.c_int
+    lib.ssb_dry_destroy.argtypes = [vp]
+    lib.ssb_dry_update.restype = ctypes.c_int
+    lib.ssb_dry_update.argtypes = [vp, vp, vp]
+    lib.ssb_dry_penalties.restype = ctypes.c_int
+    lib.ssb_dry_penalties.argtypes = [vp, i32, vp, vp, i32, ctypes.POINTER(i32), vp]
+    lib.ssb_haru_shape_rows.restype = ctypes.c_int
+    lib.ssb_haru_shape_rows.argtypes = [vp, ctypes.POINTER(HaruShape), vp, vp]
     _LIB = lib
     return lib
 
@@ -255,3 +282,58 @@ class Sampler:
         s = None if stream is None else ctypes.c_void_p(stream.cuda_stream)
         _check(self.lib, self.lib.ssb_sample_host(self.ctx, ctypes.byref(r), s))
         return ids, status
+
+
+class Dry:
+    """The DRY state of `streams` Haru text streams on the device (haru::Dry, haru/sampler.h:49-69)."""
+
+    def __init__(self, sampler: "Sampler", config: DryConfig, streams: int, exempt=()):
+        self.lib = sampler.lib
+        self.streams = streams
+        ex = np.ascontiguousarray(np.asarray(exempt, np.int32))
+        h = ctypes.c_void_p()
+        _check(self.lib, self.lib.ssb_dry_create(sampler.ctx, ctypes.byref(config), streams,
+                                                 _hptr(ex) if len(ex) else None, len(ex), ctypes.byref(h)))
+        self.h = h
+
+    def update(self, tokens, stream=None):
+        """Dry::update(tokens[s]) for every stream s; tokens: int32 device tensor [streams] (< 0: skip)."""
+        s = None if stream is None else ctypes.c_void_p(stream.cuda_stream)
+        _check(self.lib, self.lib.ssb_dry_update(self.h, _dptr(tokens), s))
+
+    def penalties(self, s: int, cap: int = 1024, stream=None):
+        """Dry::penalties() of stream s: (tokens int32, penalties float64) by rising token."""
+        t = np.empty(cap, np.int32)
+        v = np.empty(cap, np.float64)
+        n = ctypes.c_int32(0)
+        st = None if stream is None else ctypes.c_void_p(stream.cuda_stream)
+        _check(self.lib, self.lib.ssb_dry_penalties(self.h, s, _hptr(t), _hptr(v), cap, ctypes.byref(n), st))
+        k = min(n.value, cap)
+        return t[:k].copy(), v[:k].copy()
+
+    def close(self):
+        if self.h:
+            self.lib.ssb_dry_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def haru_shape(sampler: "Sampler", logits, silent, pad: int, eop: int, eos: int, eop_bias: float = 0.0,
+               must_speak=None, dry: Dry | None = None, stream=None):
+    """shape_logits() (haru/sampler.cpp:116-124) on f32 device rows [rows, V], in place."""
+    h = HaruShape()
+    h.logits = logits.data_ptr()
+    h.rows, h.vocab = logits.shape
+    h.ld = logits.stride(0)
+    h.silent = silent.data_ptr()
+    h.silent_ld = silent.stride(0)
+    h.pad, h.eop, h.eos = pad, eop, eos
+    h.eop_bias = eop_bias
+    h.must_speak = _dptr(must_speak)
+    s = None if stream is None else ctypes.c_void_p(stream.cuda_stream)
+    _check(sampler.lib, sampler.lib.ssb_haru_shape_rows(sampler.ctx, ctypes.byref(h), dry.h if dry else None, s))

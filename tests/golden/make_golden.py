@@ -2,8 +2,8 @@
 sources into oracle/_ref/libref_sampler.so (oracle/Makefile). The reference ships no vectors for this
 path (its generators, reference/qwen3-tts/sampling_cases.py and reference/haru/sampling_cases.py, need
 model dumps), so the inputs here are seeded synthetic logits shaped like those cases, and the outputs
-are what the reference's sample(), candidates(), pick(), uniform(), haru::candidates() and
-drama3::candidates() return.
+are what the reference's sample(), candidates(), pick(), uniform(), haru::candidates(),
+drama3::candidates(), haru::Dry and shape_logits() return.
 
 Run here, where the reference sources exist:   python tests/golden/make_golden.py
 The fixtures travel with the repository; the tests never need the reference at run time.
@@ -201,6 +201,48 @@ def drama3_cases(ref: RefSampler) -> dict:
     return out
 
 
+# DRY settings for the Haru fixtures (the file's dry_* keys, haru/sampler.cpp:63-73; the model's own values
+# come with its GGUF, so these are seeded stand-ins of the same kind) and the text ids they exempt.
+HARU_DRY = {"mild": (0.8, 1.75, 3.0, 2, 64, 8), "long-window": (1.0, 2.0, 50.0, 3, 512, 32),
+            "allowed-1": (0.5, 1.5, 1.0, 1, 16, 4)}
+HARU_IDS = (0, 1, 2)  # pad, eop, eos
+HARU_DRY_STEPS, HARU_DRY_CAP = 400, 64
+
+
+def haru_dry_tokens(rng, steps, vocab):
+    """A token stream with the repeats DRY looks for: runs copied from earlier, interleaved with fresh
+    tokens and the exempt text ids."""
+    out = []
+    while len(out) < steps:
+        r = rng.random()
+        if r < 0.45 and len(out) > 8:
+            start = int(rng.integers(0, len(out) - 4))
+            out.extend(out[start:start + int(rng.integers(2, 12))])
+        elif r < 0.55:
+            out.append(int(rng.choice(HARU_IDS)))
+        else:
+            out.extend(int(t) for t in rng.integers(3, vocab, size=int(rng.integers(1, 6))))
+    return np.array(out[:steps], np.int32)
+
+
+def haru_dry_cases(ref: RefSampler) -> dict:
+    """haru::Dry's penalties after every token of seeded streams, and shape_logits() of seeded rows."""
+    from oracle import DryConfig
+    out = {}
+    rng = np.random.default_rng(31)
+    for name, c in HARU_DRY.items():
+        cfg = DryConfig(*c, 0)
+        toks = haru_dry_tokens(rng, HARU_DRY_STEPS, 60)
+        pt, pv, cnt = ref.dry_run(cfg, np.array(HARU_IDS, np.int32), toks, HARU_DRY_CAP)
+        x = (rng.standard_normal((4, 4096)) * 2).astype(np.float32)
+        silent = (rng.standard_normal((4, 2)) * 2).astype(np.float32)
+        shaped = np.stack([ref.haru_shape(x[r], cfg, np.array(HARU_IDS, np.int32), toks[:100 * (r + 1)], silent[r],
+                                          *HARU_IDS, float(0.5 * r), r == 3) for r in range(4)])
+        out[name] = dict(config=np.array(c[:3]), ints=np.array(c[3:], np.int32), tokens=toks, pen_tokens=pt,
+                         pen_values=pv, counts=cnt, logits=x, silent=silent, shaped=shaped)
+    return out
+
+
 def main():
     build(ref=True)
     ref = RefSampler()
@@ -217,6 +259,9 @@ def main():
     d = drama3_cases(ref)
     np.savez_compressed(os.path.join(HERE, "drama3_cases.npz"),
                         **{f"{c}/{k}": v for c, dd in d.items() for k, v in dd.items()})
+    hd = haru_dry_cases(ref)
+    np.savez_compressed(os.path.join(HERE, "haru_dry_cases.npz"),
+                        **{f"{c}/{k}": v for c, dd in hd.items() for k, v in dd.items()})
     with open(os.path.join(HERE, "kat.json"), "w") as f:
         json.dump(kats(ref), f, indent=1)
     print("wrote", sorted(os.listdir(HERE)))

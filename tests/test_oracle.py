@@ -252,3 +252,45 @@ def test_family_agreement_with_reference(oracle, ref):
             assert a[0] == b[0], (trial, fam)
             assert np.array_equal(a[1], b[1]), (trial, fam)
             assert np.array_equal(a[2], b[2]), (trial, fam)
+
+
+# ---------------------------------------------------------------- Haru's DRY and logit shaping
+@pytest.mark.parametrize("case", ["mild", "long-window", "allowed-1"])
+def test_haru_dry_golden(oracle, case):
+    """haru::Dry (haru/sampler.cpp:82-114) after every token of the fixture's stream, and shape_logits()
+    (:116-124), as the compiled reference returned them: bit for bit."""
+    from oracle import DryConfig
+    c = load_cases("haru_dry_cases.npz")[case]
+    cfg = DryConfig(*[float(v) for v in c["config"]], *[int(v) for v in c["ints"]], 0)
+    ids = (0, 1, 2)
+    pt, pv, cnt = oracle.dry_run(cfg, np.array(ids, np.int32), c["tokens"], c["pen_tokens"].shape[1])
+    assert np.array_equal(cnt, c["counts"])
+    assert np.array_equal(pt, c["pen_tokens"]) and np.array_equal(pv, c["pen_values"])
+    for r in range(4):
+        n = 100 * (r + 1)
+        k = int(cnt[n - 1])
+        got = oracle.haru_shape(c["logits"][r], pt[n - 1, :k], pv[n - 1, :k], c["silent"][r], *ids, 0.5 * r, r == 3)
+        assert np.array_equal(got, c["shaped"][r], equal_nan=True)
+
+
+def test_haru_dry_agreement_with_reference(oracle, ref):
+    """Random streams with repeats, random settings: the restatement's penalties equal the reference's
+    after every token."""
+    from oracle import DryConfig
+    rng = np.random.default_rng(404)
+    for trial in range(40):
+        cfg = DryConfig(float(rng.choice([0.5, 0.8, 1.0])), float(rng.choice([1.2, 1.75, 2.0])),
+                        float(rng.choice([0.5, 3.0, 1e9])), int(rng.choice([0, 1, 2, 3, 5])),
+                        int(rng.choice([0, 1, 8, 64, 300])), int(rng.choice([0, 1, 4, 16, 64])), 0)
+        vocab = int(rng.choice([4, 20, 200]))
+        toks = rng.integers(0, vocab, size=300).astype(np.int32)
+        for _ in range(20):  # copied runs
+            a, b = sorted(rng.integers(0, 300, size=2))
+            L = int(rng.integers(2, 20))
+            if b + L <= 300 and a + L <= b:
+                toks[b:b + L] = toks[a:a + L]
+        exempt = np.array(rng.choice(vocab, size=int(rng.integers(0, 3)), replace=False), np.int32)
+        got = oracle.dry_run(cfg, exempt, toks, 128)
+        want = ref.dry_run(cfg, exempt, toks, 128)
+        for g, w in zip(got, want):
+            assert np.array_equal(g, w), trial
