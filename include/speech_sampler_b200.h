@@ -221,6 +221,30 @@ SSB_API ssb_status ssb_sample_host(ssb_context *ctx, const ssb_rows *rows, void 
  */
 SSB_API ssb_status ssb_sample_rows_noalloc(const ssb_rows *rows, void *stream);
 
+/* ---------------------------------------------------------------- device-resident chains */
+
+/*
+ * The embedding rows of the drawn ids (ggml_get_rows of the next step's table, as the code predictor's
+ * chain feeds each pick to the next codebook: src/families/qwen3-tts/talker.cpp:58-64): after the rows
+ * are sampled, out[r, 0:dim] = table[ids[r], 0:dim]; a row whose status is not SSB_ROW_OK (or whose id
+ * is outside [0, table_rows)) gets zeros. Everything stays on the device and in stream order, so a
+ * chain of steps can be captured into one CUDA graph with no readback between picks.
+ */
+typedef struct ssb_embed {
+    const void *table;  /* [table_rows, ld] device */
+    int64_t ld;         /* elements between table rows (>= dim) */
+    int32_t table_rows;
+    int32_t dtype;      /* ssb_dtype of table and out */
+    int32_t dim;        /* elements per embedding row */
+    int32_t reserved;   /* must be 0 */
+    void *out;          /* [rows, out_ld] device */
+    int64_t out_ld;     /* elements between out rows (>= dim) */
+} ssb_embed;
+
+/* ssb_sample_rows, then the embedding rows of the drawn ids (ids and status are written as usual). */
+SSB_API ssb_status ssb_sample_embed_rows(ssb_context *ctx, const ssb_rows *rows, const ssb_embed *embed,
+                                         void *stream);
+
 /* ---------------------------------------------------------------- Haru's logit shaping and DRY */
 
 /* DryConfig (haru/sampler.h:37-40, read by file_dry, haru/sampler.cpp:63-73). */

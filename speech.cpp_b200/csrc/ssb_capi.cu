@@ -457,6 +457,30 @@ ssb_status ssb_sample_rows(ssb_context * ctx, const ssb_rows * rows, void * stre
     return run(ctx, rows, nullptr, static_cast<cudaStream_t>(stream));
 }
 
+ssb_status ssb_sample_embed_rows(ssb_context * ctx, const ssb_rows * rows, const ssb_embed * e, void * stream) {
+    if (!e) return fail(SSB_INVALID_ARGUMENT, "embed is required");
+    if (e->reserved != 0) return fail(SSB_INVALID_ARGUMENT, "reserved fields must be 0");
+    if (e->dtype != SSB_F32 && e->dtype != SSB_BF16) return fail(SSB_INVALID_ARGUMENT, "embed dtype is neither SSB_F32 nor SSB_BF16");
+    if (e->dim < 1 || e->table_rows < 1 || e->ld < e->dim || e->out_ld < e->dim)
+        return fail(SSB_INVALID_ARGUMENT, "embed dim, table_rows, ld or out_ld out of order");
+    if (!e->table || !e->out) return fail(SSB_INVALID_ARGUMENT, "embed table and out are required");
+    const ssb_status s = run(ctx, rows, nullptr, static_cast<cudaStream_t>(stream));
+    if (s != SSB_OK || rows->rows == 0) return s;
+    ssb::EmbedArgs a{};
+    a.table = e->table;
+    a.ld = e->ld;
+    a.table_rows = e->table_rows;
+    a.dim = e->dim;
+    a.out = e->out;
+    a.out_ld = e->out_ld;
+    a.ids = rows->ids;
+    a.status = rows->status;
+    a.rows = rows->rows;
+    const cudaError_t err = ssb::launch_embed(a, e->dtype == SSB_BF16, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "embedding launch");
+    return ok();
+}
+
 ssb_status ssb_candidates_rows(ssb_context * ctx, const ssb_rows * rows, int32_t cap, int32_t * tokens, double * weights,
                                int32_t * count, float * processed, void * stream) {
     if (cap < 0) return fail(SSB_INVALID_ARGUMENT, "cap is negative");

@@ -103,6 +103,20 @@ struct FlavorArgs {
 size_t flavor_smem_bytes(int cap, int bit_words, int hist_slots);
 cudaError_t launch_flavor(const FlavorArgs & a, bool bf16, bool debug, cudaStream_t stream);
 
+// The embedding rows of drawn ids (ssb_embed.cu): out[r] = table[ids[r]] (zeros for a refused row).
+struct EmbedArgs {
+    const void * table;
+    int64_t ld;
+    int table_rows;
+    int dim;
+    void * out;
+    int64_t out_ld;
+    const int32_t * ids;
+    const int32_t * status;
+    int rows;
+};
+cudaError_t launch_embed(const EmbedArgs & a, bool bf16, cudaStream_t stream);
+
 // Haru's DRY state update and logit shaping (ssb_haru.cu).
 struct DryConfigD {
     double multiplier, base, max_penalty;

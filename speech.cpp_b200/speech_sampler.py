@@ -97,6 +97,13 @@ class HaruShape(ctypes.Structure):
                 ("eop_bias", ctypes.c_float), ("must_speak", ctypes.c_void_p)]
 
 
+class Embed(ctypes.Structure):
+    """ssb_embed: the table the drawn ids index (ggml_get_rows of the chain's next step)."""
+    _fields_ = [("table", ctypes.c_void_p), ("ld", ctypes.c_int64), ("table_rows", ctypes.c_int32),
+                ("dtype", ctypes.c_int32), ("dim", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("out", ctypes.c_void_p), ("out_ld", ctypes.c_int64)]
+
+
 def header_symbols(path: str = HEADER):
     """Every function the C header declares (SSB_API ... name(...))."""
     text = open(path).read()
@@ -131,6 +138,8 @@ def load_library(path: str = LIB_PATH):
     lib.ssb_sample_host.argtypes = [vp, ctypes.POINTER(Rows), vp]
     lib.ssb_restrict_rows.restype = ctypes.c_int
     lib.ssb_restrict_rows.argtypes = [vp, ctypes.POINTER(Rows), vp, ctypes.c_int64, vp]
+    lib.ssb_sample_embed_rows.restype = ctypes.c_int
+    lib.ssb_sample_embed_rows.argtypes = [vp, ctypes.POINTER(Rows), ctypes.POINTER(Embed), vp]
     lib.ssb_context_mask.restype = ctypes.c_int
     lib.ssb_context_mask.argtypes = [vp, vp, ctypes.c_int64, ctypes.POINTER(vp)]
     lib.ssb_dry_create.restype = ctypes.c_int
@@ -236,6 +245,29 @@ class Sampler:
         r = self._rows_struct(logits, p, history, history_len, mask, mask_kind, u, ids, status, row_params, max_top_k)
         s = None if stream is None else ctypes.c_void_p(stream.cuda_stream)
         _check(self.lib, self.lib.ssb_sample_rows(self.ctx, ctypes.byref(r), s))
+        return ids, status
+
+    def sample_embed(self, logits, p: Params | None, table, out, u=None, history=None, history_len=None, mask=None,
+                     mask_kind=MASK_NONE, ids=None, status=None, stream=None):
+        """sample(), then out[r] = table[ids[r]] on the device (zeros for a refused row)."""
+        import torch
+        b = logits.shape[0]
+        if ids is None:
+            ids = torch.empty(b, dtype=torch.int32, device=logits.device)
+        if status is None:
+            status = torch.empty(b, dtype=torch.int32, device=logits.device)
+        r = self._rows_struct(logits, p, history, history_len, mask, mask_kind, u, ids, status)
+        e = Embed()
+        e.table = table.data_ptr()
+        e.table_rows, e.dim = table.shape
+        e.ld = table.stride(0)
+        e.dtype = BF16 if table.dtype == torch.bfloat16 else F32
+        if out.dtype != table.dtype or out.shape[1] < e.dim:
+            raise ValueError("out must have the table's dtype and at least its width")
+        e.out = out.data_ptr()
+        e.out_ld = out.stride(0)
+        s = None if stream is None else ctypes.c_void_p(stream.cuda_stream)
+        _check(self.lib, self.lib.ssb_sample_embed_rows(self.ctx, ctypes.byref(r), ctypes.byref(e), s))
         return ids, status
 
     def candidates(self, logits, p: Params | None = None, history=None, history_len=None, mask=None,

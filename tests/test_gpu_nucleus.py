@@ -130,3 +130,36 @@ def test_reserve_then_graph_capture(oracle):
         del g
     finally:
         s.close()
+
+
+@pytest.mark.parametrize("density", [0.001, 0.5])
+def test_config5_batch_4096(engine, oracle, density):
+    """Configuration 5 at its largest batch, B = 4096 rows of 151936 tokens (2.5 GB of fp32 logits): more
+    rows than the grid holds CTAs, so every CTA loops over rows and reuses its candidate-list region. 64
+    rows spread over the batch (the first and last, and rows past each multiple of the grid) are checked
+    against the oracle; every status must be OK."""
+    c = wl.config5(rows=4096, density=density)
+    p = params(**c["params"])
+    ids, st = engine_run(engine, c["logits"], ss.params(**c["params"]), mask=c["mask"], mask_kind=MASK_ALLOW, u=c["u"])
+    assert np.all(st == ss.ROW_OK)
+    rng = np.random.default_rng(7)
+    pick = np.unique(np.concatenate([[0, 1, 147, 148, 149, 295, 296, 297, 1023, 2048, 4094, 4095],
+                                     rng.choice(4096, 52, replace=False)]))[:64]
+    want, wst, _ = oracle.sample_rows(c["logits"][pick], p, mask=c["mask"][pick], mask_kind=MASK_ALLOW,
+                                      u=c["u"][pick])
+    near = assert_ids(oracle, ids[pick], st[pick], want, wst, c["logits"][pick], lambda r: p, lambda r: None,
+                      lambda r: c["mask"][pick][r], MASK_ALLOW, c["u"][pick])
+    assert near == 0
+
+
+@pytest.mark.parametrize("density", [0.001, 0.01, 0.1, 0.5])
+def test_config5_batch_1(engine, oracle, density):
+    """Configuration 5 at B = 1: one-row calls (one CTA for the whole row), 16 rows per density, each
+    against the oracle."""
+    c = wl.config5(rows=16, density=density, row0=5000)
+    p = params(**c["params"])
+    for r in range(16):
+        ids, st = engine_run(engine, c["logits"][r:r + 1], ss.params(**c["params"]), mask=c["mask"][r:r + 1],
+                             mask_kind=MASK_ALLOW, u=c["u"][r:r + 1])
+        o = oracle.sample_row(c["logits"][r], p, None, c["mask"][r], MASK_ALLOW, c["u"][r])
+        assert st[0] == o["status"] == ss.ROW_OK and ids[0] == o["id"], (r, ids[0], o["id"])
