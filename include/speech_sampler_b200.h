@@ -245,6 +245,30 @@ typedef struct ssb_embed {
 SSB_API ssb_status ssb_sample_embed_rows(ssb_context *ctx, const ssb_rows *rows, const ssb_embed *embed,
                                          void *stream);
 
+/*
+ * The LM head fused with the greedy pick (Qwen3Readback::Pick, src/common/qwen3-decoder.cpp:422-437, and
+ * verify()'s argmax over [n, vocab], :492-510): ids[r] = the first maximum over tokens v of
+ * hidden[r] . weight[v], with bf16 inputs and fp32 accumulation on the tensor cores; the logits are never
+ * written. rows 1..256, dim a multiple of 64, hidden_ld and weight_ld multiples of 8 elements, both base
+ * pointers 16-byte aligned. max_logit (the winning logit) and status are optional. Calls on one context
+ * must not overlap on the GPU (they share the context's per-row maxima).
+ */
+typedef struct ssb_lm_head {
+    const void *hidden;  /* [rows, hidden_ld] bf16 device */
+    int64_t hidden_ld;
+    int32_t rows;
+    int32_t dim;
+    const void *weight;  /* [vocab, weight_ld] bf16 device: one row per token */
+    int64_t weight_ld;
+    int32_t vocab;
+    int32_t dtype;       /* SSB_BF16 */
+    int32_t *ids;        /* [rows] */
+    float *max_logit;    /* [rows] or null */
+    int32_t *status;     /* [rows] or null: SSB_ROW_OK, or SSB_ROW_DEVICE_TIMEOUT */
+} ssb_lm_head;
+
+SSB_API ssb_status ssb_lm_head_argmax(ssb_context *ctx, const ssb_lm_head *head, void *stream);
+
 /* ---------------------------------------------------------------- Haru's logit shaping and DRY */
 
 /* DryConfig (haru/sampler.h:37-40, read by file_dry, haru/sampler.cpp:63-73). */

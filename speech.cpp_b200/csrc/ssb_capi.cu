@@ -40,6 +40,9 @@ struct ssb_context {
     size_t occ_topk_smem[3][2] = {};  // the shared memory each was measured at
     // device copies of caller masks (ssb_context_mask), freed with the context
     std::vector<void *> masks;
+    // the fused LM-head argmax: per-row composite maxima and the error word, zero between calls
+    uint64_t * lm_best = nullptr;  // [kLmMaxRows]
+    int32_t * lm_error = nullptr;
 };
 
 // The DRY state of Haru's text streams (one device allocation).
@@ -374,6 +377,9 @@ ssb_status ssb_context_create(int32_t device, ssb_context ** out) {
     if (e == cudaSuccess) e = cudaMalloc(&ctx->part_flags, ms * sizeof(int32_t));
     if (e == cudaSuccess) e = cudaMalloc(&ctx->counters, ms * sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaMemset(ctx->counters, 0, ms * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->lm_best, ssb::kLmMaxRows * sizeof(uint64_t) + 16);
+    if (e == cudaSuccess) e = cudaMemset(ctx->lm_best, 0, ssb::kLmMaxRows * sizeof(uint64_t) + 16);
+    if (e == cudaSuccess) ctx->lm_error = reinterpret_cast<int32_t *>(ctx->lm_best + ssb::kLmMaxRows);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->done, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
@@ -397,6 +403,7 @@ ssb_status ssb_context_destroy(ssb_context * ctx) {
     cudaFree(ctx->stage);
     cudaFree(ctx->nuc_scratch);
     for (void * m : ctx->masks) cudaFree(m);
+    cudaFree(ctx->lm_best);
     if (ctx->done) cudaEventDestroy(ctx->done);
     if (cur >= 0) cudaSetDevice(cur);
     delete ctx;
@@ -478,6 +485,40 @@ ssb_status ssb_sample_embed_rows(ssb_context * ctx, const ssb_rows * rows, const
     a.rows = rows->rows;
     const cudaError_t err = ssb::launch_embed(a, e->dtype == SSB_BF16, static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return cuda_fail(err, "embedding launch");
+    return ok();
+}
+
+ssb_status ssb_lm_head_argmax(ssb_context * ctx, const ssb_lm_head * h, void * stream) {
+    if (!ctx || !h) return fail(SSB_INVALID_ARGUMENT, "ctx and head are required");
+    if (h->dtype != SSB_BF16) return fail(SSB_INVALID_ARGUMENT, "the LM head takes bf16 hidden rows and weights");
+    if (h->rows < 1 || h->rows > ssb::kLmMaxRows) return fail(SSB_OUT_OF_RANGE, "rows must lie in [1, 256]");
+    if (h->dim < 64 || h->dim % 64 != 0) return fail(SSB_INVALID_ARGUMENT, "dim must be a positive multiple of 64");
+    if (h->vocab < 1 || h->vocab > SSB_MAX_VOCAB) return fail(SSB_OUT_OF_RANGE, "vocab must lie in [1, SSB_MAX_VOCAB]");
+    if (h->hidden_ld < h->dim || h->weight_ld < h->dim || h->hidden_ld % 8 != 0 || h->weight_ld % 8 != 0)
+        return fail(SSB_INVALID_ARGUMENT, "hidden_ld and weight_ld must be at least dim and multiples of 8");
+    if (!h->hidden || !h->weight || !h->ids) return fail(SSB_INVALID_ARGUMENT, "hidden, weight and ids are required");
+    if ((reinterpret_cast<uintptr_t>(h->hidden) | reinterpret_cast<uintptr_t>(h->weight)) % 16 != 0)
+        return fail(SSB_INVALID_ARGUMENT, "hidden and weight must be 16-byte aligned");
+    ssb_status st = use_device(ctx);
+    if (st != SSB_OK) return st;
+    ssb::LmArgs a{};
+    a.rows = h->rows;
+    a.vocab = h->vocab;
+    a.dim = h->dim;
+    a.n_pad = (h->rows + 15) / 16 * 16;
+    a.stages = ssb::lm_stages(a.n_pad, (size_t) ctx->max_smem);
+    if (a.stages < 2) return fail(SSB_OUT_OF_RANGE, "the LM head's stages need more shared memory than the device has");
+    a.tmem_cols = ssb::next_pow2(std::max(32, 2 * a.n_pad));
+    a.best = ctx->lm_best;
+    a.error = ctx->lm_error;
+    a.ids = h->ids;
+    a.max_logit = h->max_logit;
+    a.status = h->status;
+    const int tiles = (h->vocab + 127) / 128;
+    const int grid = std::min(tiles, ctx->sm_count);
+    const cudaError_t e = ssb::launch_lm_argmax(a, h->hidden, h->hidden_ld, h->weight, h->weight_ld, grid,
+                                                static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "LM-head launch");
     return ok();
 }
 

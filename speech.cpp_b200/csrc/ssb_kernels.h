@@ -103,6 +103,22 @@ struct FlavorArgs {
 size_t flavor_smem_bytes(int cap, int bit_words, int hist_slots);
 cudaError_t launch_flavor(const FlavorArgs & a, bool bf16, bool debug, cudaStream_t stream);
 
+// The LM head fused with its argmax (ssb_lmhead.cu): tcgen05 MMAs over 128-token tiles, the argmax in the
+// TMEM epilogue. n_pad = rows rounded up to 16 (the MMA's N); tmem_cols = two accumulators of n_pad.
+struct LmArgs {
+    int rows, vocab, dim, n_pad, stages, tmem_cols;
+    uint64_t * best;    // [n_pad] composite maxima, 0 between calls
+    int32_t * error;    // 0 between calls
+    int32_t * ids;
+    float * max_logit;  // or null
+    int32_t * status;   // or null
+};
+constexpr int kLmMaxRows = 256;
+int lm_stages(int n_pad, size_t max_smem);
+size_t lm_smem_bytes(int n_pad, int stages);
+cudaError_t launch_lm_argmax(const LmArgs & a, const void * hidden, int64_t hidden_ld, const void * weight,
+                             int64_t weight_ld, int grid, cudaStream_t stream);
+
 // The embedding rows of drawn ids (ssb_embed.cu): out[r] = table[ids[r]] (zeros for a refused row).
 struct EmbedArgs {
     const void * table;

@@ -104,6 +104,14 @@ class Embed(ctypes.Structure):
                 ("out", ctypes.c_void_p), ("out_ld", ctypes.c_int64)]
 
 
+class LmHead(ctypes.Structure):
+    """ssb_lm_head: the LM head fused with its argmax."""
+    _fields_ = [("hidden", ctypes.c_void_p), ("hidden_ld", ctypes.c_int64), ("rows", ctypes.c_int32),
+                ("dim", ctypes.c_int32), ("weight", ctypes.c_void_p), ("weight_ld", ctypes.c_int64),
+                ("vocab", ctypes.c_int32), ("dtype", ctypes.c_int32), ("ids", ctypes.c_void_p),
+                ("max_logit", ctypes.c_void_p), ("status", ctypes.c_void_p)]
+
+
 def header_symbols(path: str = HEADER):
     """Every function the C header declares (SSB_API ... name(...))."""
     text = open(path).read()
@@ -138,6 +146,8 @@ def load_library(path: str = LIB_PATH):
     lib.ssb_sample_host.argtypes = [vp, ctypes.POINTER(Rows), vp]
     lib.ssb_restrict_rows.restype = ctypes.c_int
     lib.ssb_restrict_rows.argtypes = [vp, ctypes.POINTER(Rows), vp, ctypes.c_int64, vp]
+    lib.ssb_lm_head_argmax.restype = ctypes.c_int
+    lib.ssb_lm_head_argmax.argtypes = [vp, ctypes.POINTER(LmHead), vp]
     lib.ssb_sample_embed_rows.restype = ctypes.c_int
     lib.ssb_sample_embed_rows.argtypes = [vp, ctypes.POINTER(Rows), ctypes.POINTER(Embed), vp]
     lib.ssb_context_mask.restype = ctypes.c_int
@@ -269,6 +279,21 @@ class Sampler:
         s = None if stream is None else ctypes.c_void_p(stream.cuda_stream)
         _check(self.lib, self.lib.ssb_sample_embed_rows(self.ctx, ctypes.byref(r), ctypes.byref(e), s))
         return ids, status
+
+    def lm_head_argmax(self, hidden, weight, ids=None, max_logit=None, status=None, stream=None):
+        """ids[r] = first argmax over tokens of hidden[r] . weight[v] (bf16 in, fp32 accumulation), fused."""
+        import torch
+        rows, dim = hidden.shape
+        if ids is None:
+            ids = torch.empty(rows, dtype=torch.int32, device=hidden.device)
+        h = LmHead()
+        h.hidden, h.hidden_ld, h.rows, h.dim = hidden.data_ptr(), hidden.stride(0), rows, dim
+        h.weight, h.weight_ld, h.vocab = weight.data_ptr(), weight.stride(0), weight.shape[0]
+        h.dtype = BF16 if hidden.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 else F32
+        h.ids, h.max_logit, h.status = ids.data_ptr(), _dptr(max_logit), _dptr(status)
+        s = None if stream is None else ctypes.c_void_p(stream.cuda_stream)
+        _check(self.lib, self.lib.ssb_lm_head_argmax(self.ctx, ctypes.byref(h), s))
+        return ids
 
     def candidates(self, logits, p: Params | None = None, history=None, history_len=None, mask=None,
                    mask_kind=MASK_NONE, u=None, row_params=None, max_top_k=0, cap=64, processed=True, stream=None):
