@@ -53,6 +53,10 @@ def parse_args():
     ap.add_argument("--density", type=float, default=0.01, help="config 5 allow-mask density")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--path", choices=["sample", "lm-head", "chain"], default="sample",
+                    help="sample: the sampler on --config (the headline); lm-head: the fused LM head + argmax "
+                         "(--rows, --dim) against cuBLAS + argmax; chain: the device-resident code-predictor chain")
+    ap.add_argument("--dim", type=int, default=2048, help="lm-head: hidden size")
     ap.add_argument("--launches-only", type=int, default=0,
                     help="profiling aid: after the oracle check, issue this many launches and exit (no timing, no JSON)")
     return ap.parse_args()
@@ -209,10 +213,134 @@ def run_reference(args):
 
 
 # ---------------------------------------------------------------- the engine
+def _events_time(torch, fn, steps, warmup, stream):
+    """ms per call of fn() on `stream`, CUDA events around `steps` calls after `warmup` untimed ones."""
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            fn()
+        stream.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(steps):
+            fn()
+        b.record(stream)
+    b.synchronize()
+    return a.elapsed_time(b) / steps
+
+
+def run_lm_head(args):
+    """The fused LM head + argmax (ssb_lm_head_argmax) on bf16 hidden rows [R, dim] and a Qwen3-vocabulary
+    head [151936, dim]: rows/s, HBM roofline on the head's bytes (read once per call), tensor FLOP/s, and
+    the unfused cuBLAS GEMM + argmax on the same inputs beside it. A pool of heads larger than twice L2
+    keeps every call's weights out of L2."""
+    import torch
+    import speech_sampler as ss
+    torch.cuda.set_device(0)
+    rows, dim, vocab = max(1, args.rows or 1), args.dim, wl.QWEN3_VOCAB
+    g = torch.Generator(device="cuda").manual_seed(1)
+    head_bytes = vocab * dim * 2
+    pool_n = max(2, int(math.ceil(2 * L2_BYTES / head_bytes)) + 1)
+    heads = [(torch.randn(vocab, dim, device="cuda", generator=g) * (2.0 / dim ** 0.5)).to(torch.bfloat16)
+             for _ in range(pool_n)]
+    hidden = torch.randn(rows, dim, device="cuda", generator=g).to(torch.bfloat16)
+    sampler = ss.Sampler(0)
+    ids = torch.empty(rows, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.Stream()
+    it = [0]
+
+    def fused():
+        sampler.lm_head_argmax(hidden, heads[it[0] % pool_n], ids, stream=stream)
+        it[0] += 1
+
+    def unfused():
+        torch.argmax(hidden @ heads[it[0] % pool_n].T, dim=1)
+        it[0] += 1
+
+    with torch.cuda.stream(stream):
+        fused()
+    stream.synchronize()
+    ref = torch.argmax(hidden.float() @ heads[0].float().T, dim=1).to(torch.int32)
+    agree = float((ids == ref).float().mean())
+    clocks = Clocks(0)
+    clocks.start()
+    ms = _events_time(torch, fused, args.steps, max(3, args.warmup), stream)
+    clk = clocks.stop()
+    ms_unfused = _events_time(torch, unfused, max(20, args.steps // 10), 3, stream)
+    hbm, src = peaks()
+    try:
+        tflops_peak = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"])
+    except Exception:
+        tflops_peak = 1590.0
+    gbs = (head_bytes + rows * dim * 2) / (ms * 1e-3) / 1e9
+    tfs = 2.0 * rows * vocab * dim / (ms * 1e-3) / 1e12
+    print(json.dumps({
+        "metric": "LM-head argmax rows/sec", "value": rows / (ms * 1e-3), "unit": "rows/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True,
+        "dtype": "bf16 (fp32 accumulate)", "data": "synthetic",
+        "config": {"workload": f"hidden [{rows}, {dim}] x head [{vocab}, {dim}] -> argmax",
+                   "l2": f"pool of {pool_n} heads > 2x L2"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                     "peak_source": src, "tensor_tflops": tfs, "tensor_frac": tfs / tflops_peak},
+        "unfused_cublas_argmax_ms": ms_unfused, "speedup_vs_unfused": ms_unfused / ms,
+        "ids_agree_with_fp32_torch": agree, "clocks": clk}))
+    sampler.close()
+
+
+def run_chain(args):
+    """The code predictor's 15-codebook chain for 64 streams (config 3's shape: [64, 2048] per step, T 0.9,
+    top-k 50): per step a GEMV of the previous pick's embedding rows (hidden 1024) gives the logits and
+    ssb_sample_embed_rows draws and gathers the next input, all captured in one CUDA graph (one replay =
+    one frame of 64 streams). Beside it the same chain with the ids read back to the host after every
+    step, as a host-sampled loop must."""
+    import torch
+    import speech_sampler as ss
+    torch.cuda.set_device(0)
+    B, H, V, G = 64, 1024, wl.CP_VOCAB, 15
+    g = torch.Generator(device="cuda").manual_seed(3)
+    W = torch.randn(G, H, V, device="cuda", generator=g).to(torch.bfloat16) * (1.5 / H ** 0.5)
+    E = torch.randn(G, V, H, device="cuda", generator=g).to(torch.bfloat16)
+    h = torch.randn(G + 1, B, H, device="cuda", generator=g).to(torch.bfloat16)
+    u = torch.rand(G, B, device="cuda", generator=g, dtype=torch.float64)
+    logits = torch.empty(G, B, V, device="cuda")
+    ids = torch.empty(G, B, dtype=torch.int32, device="cuda")
+    st = torch.empty(G, B, dtype=torch.int32, device="cuda")
+    sampler = ss.Sampler(0)
+    p = ss.params(temperature=0.9, top_k=50, top_p=1.0)
+    stream = torch.cuda.Stream()
+
+    def chain(readback=False):
+        for step in range(G):
+            logits[step].copy_(h[step] @ W[step])
+            sampler.sample_embed(logits[step], p, E[step], h[step + 1], u=u[step], ids=ids[step], status=st[step],
+                                 stream=torch.cuda.current_stream())
+            if readback:
+                ids[step].cpu()
+
+    with torch.cuda.stream(stream):
+        chain()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        chain()
+    ms_graph = _events_time(torch, graph.replay, args.steps, max(3, args.warmup), stream)
+    ms_eager = _events_time(torch, lambda: chain(True), max(10, args.steps // 20), 3, stream)
+    print(json.dumps({
+        "metric": "code-predictor frames/sec (64 streams x 15 codebooks)", "value": 1e3 / ms_graph,
+        "unit": "frames/s", "n_gpus": 1, "steps": args.steps, "ms_per_step": ms_graph, "higher_is_better": True,
+        "dtype": "f32 logits, bf16 tables", "data": "synthetic",
+        "config": {"workload": "15 x ([64, 1024] x [1024, 2048] GEMV -> sample top-k 50 -> gather [64, 1024])"},
+        "readback_per_step_ms": ms_eager, "speedup_vs_readback": ms_eager / ms_graph}))
+    sampler.close()
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.path == "lm-head":
+        return run_lm_head(args)
+    if args.path == "chain":
+        return run_chain(args)
     rank, local_rank, world = dist_env()
     import torch
     import torch.distributed as dist

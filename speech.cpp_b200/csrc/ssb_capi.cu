@@ -514,8 +514,10 @@ ssb_status ssb_lm_head_argmax(ssb_context * ctx, const ssb_lm_head * h, void * s
     a.ids = h->ids;
     a.max_logit = h->max_logit;
     a.status = h->status;
+    // every CTA the same number of tiles (a last wave of a few tiles would run with HBM half idle)
     const int tiles = (h->vocab + 127) / 128;
-    const int grid = std::min(tiles, ctx->sm_count);
+    const int per = (tiles + ctx->sm_count - 1) / ctx->sm_count;
+    const int grid = (tiles + per - 1) / per;
     const cudaError_t e = ssb::launch_lm_argmax(a, h->hidden, h->hidden_ld, h->weight, h->weight_ld, grid,
                                                 static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "LM-head launch");

@@ -10,10 +10,11 @@
 //              tcgen05.mma kind::f16 (M = 128 tokens, N = padded rows, K = 16) per 16 columns of the slice,
 //              and tcgen05.commit frees the stage, or marks the accumulator full after the last slice.
 //   warps 2-5  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes 32 (w % 4) ...), each
-//              (row, token) logit folded into a composite key order_key(logit) << 32 | ~token, the warp's
-//              maximum per row merged into the CTA's shared maximum with a 64-bit atomicMax (ties: lowest
-//              token, as max_element / ggml_argmax take the first), and the CTA's into best[row] once at
-//              the end. The accumulator is handed back while the next tile's MMAs run into the other one.
+//              (row, token) logit folded into a composite key order_key(logit) << 32 | ~token (ties: lowest
+//              token, as max_element / ggml_argmax take the first), a warp transpose-reduce per 16 rows,
+//              and running maxima in registers across the CTA's tiles; the CTA's maxima go into best[row]
+//              with one 64-bit atomicMax per row at the end. The accumulator is handed back while the next
+//              tile's MMAs run into the other one.
 // lm_finish_kernel turns best[] into ids, the maximum logits and statuses, and clears best[] for the next
 // call. Every mbarrier wait is bounded (mbar_wait): a wait that gives up sets the error word, every role
 // leaves its loop, the issued copies and MMAs are waited for (bounded again) and the tensor memory is
@@ -191,8 +192,15 @@ __global__ void __launch_bounds__(kLmThreads, 1)
             }
         }
     } else {
-        // ---- epilogue (warps 2-5: TMEM lanes 32 (warp % 4) ...)
+        // ---- epilogue (warps 2-5: TMEM lanes 32 (warp % 4) ...). Per 16 columns (rows of hidden) a
+        // transpose-reduce over the warp leaves lane L with the maximum of column L & 15 over the warp's 32
+        // tokens (16 exchanges instead of 5 per column); lane L keeps a running maximum per 16-column chunk
+        // across all of the CTA's tiles, merged into s_best once at the end.
         const int q = warp & 3;
+        const int chunks = (a.rows + 15) / 16;
+        uint64_t run[kLmMaxRows / 16];
+#pragma unroll
+        for (int ch = 0; ch < kLmMaxRows / 16; ch++) run[ch] = 0ull;
         int tc = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, tc++) {
             const int acc = tc & 1;
@@ -207,20 +215,42 @@ __global__ void __launch_bounds__(kLmThreads, 1)
             const int token = t * kLmTileM + q * 32 + lane;
             const bool valid = token < a.vocab;
             const uint32_t base = tmem + ((uint32_t) (q * 32) << 16) + (uint32_t) (acc * N);
-            for (int c0 = 0; c0 < a.rows; c0 += 16) {
-                float v[16];
-                tmem_ld16(base + (uint32_t) c0, v);
 #pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    if (c0 + j >= a.rows) break;
-                    uint64_t key = valid ? composite(v[j], (uint32_t) token) : 0ull;
-                    key = warp_max_u64(key);
-                    if (lane == 0) atomicMax(reinterpret_cast<unsigned long long *>(&s_best[c0 + j]), (unsigned long long) key);
+            for (int ch = 0; ch < kLmMaxRows / 16; ch++) {
+                if (ch >= chunks) break;
+                float v[16];
+                tmem_ld16(base + (uint32_t) (ch * 16), v);
+                uint64_t k[16];
+#pragma unroll
+                for (int j = 0; j < 16; j++) k[j] = valid ? composite(v[j], (uint32_t) token) : 0ull;
+                // round o (8, 4, 2, 1): a lane with bit o keeps the upper half of its m keys, the other the
+                // lower, each taking the partner's copy of the half it keeps
+#pragma unroll
+                for (int o = 8, m = 16; o >= 1; o >>= 1, m >>= 1) {
+                    const bool upper = (lane & o) != 0;
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        if (i >= m / 2) break;
+                        const uint64_t send = upper ? k[i] : k[i + m / 2];
+                        const uint64_t keep = upper ? k[i + m / 2] : k[i];
+                        const uint64_t got = shfl_xor(send, o);
+                        k[i] = keep > got ? keep : got;
+                    }
                 }
+                const uint64_t other = shfl_xor(k[0], 16);  // the other half-warp's 16 tokens
+                const uint64_t best = k[0] > other ? k[0] : other;
+                run[ch] = run[ch] > best ? run[ch] : best;
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+        // lane L < 16 holds column ch * 16 + L of every chunk
+#pragma unroll
+        for (int ch = 0; ch < kLmMaxRows / 16; ch++) {
+            const int c = ch * 16 + lane;
+            if (ch < chunks && lane < 16 && c < a.rows && run[ch])
+                atomicMax(reinterpret_cast<unsigned long long *>(&s_best[c]), (unsigned long long) run[ch]);
         }
     }
     __syncthreads();
