@@ -269,6 +269,31 @@ typedef struct ssb_lm_head {
 
 SSB_API ssb_status ssb_lm_head_argmax(ssb_context *ctx, const ssb_lm_head *head, void *stream);
 
+/* ---------------------------------------------------------------- vocabulary-sharded rows */
+
+/*
+ * A row whose columns are split over several GPUs (a tensor-parallel LM head) is sampled from each
+ * rank's best candidates instead of the whole row: step 1 on every rank (ssb_shard_select), one
+ * all-gather of the records (ssb_shard_sample does it over NCCL, speech_sampler_b200_nccl.h), step 2 on
+ * every rank (ssb_shard_merge), which writes the same ids and statuses on every rank as ssb_sample_rows
+ * on the whole rows. A record holds k_cap composites per row plus one word (k_cap a power of two in
+ * [1, 1024], at least every drawing row's effective top-k; greedy rows need 1); rows that keep more
+ * (top_k 0 over a large vocabulary) come back SSB_ROW_INVALID_ROW.
+ */
+/* words (uint64) of one rank's records: rows * (k_cap + 1) */
+SSB_API int64_t ssb_shard_record_words(int32_t rows, int32_t k_cap);
+
+/* Step 1: `slice` holds columns [col_offset, col_offset + slice->vocab) of rows of vocab_total tokens
+ * (col_offset a multiple of 32); its history holds the rows' GLOBAL token ids and its mask (if any) the
+ * whole rows' mask words. Writes rows * (k_cap + 1) words to `records` (device). */
+SSB_API ssb_status ssb_shard_select(ssb_context *ctx, const ssb_rows *slice, int32_t col_offset, int32_t vocab_total,
+                                    int32_t k_cap, uint64_t *records, void *stream);
+
+/* Step 2: `records` = the world ranks' records one after another ([world][rows][k_cap + 1], device);
+ * rows' params / row_params, u, ids and status are used (its logits, history and mask are not). */
+SSB_API ssb_status ssb_shard_merge(ssb_context *ctx, const ssb_rows *rows, int32_t vocab_total, int32_t world,
+                                   int32_t k_cap, const uint64_t *records, void *stream);
+
 /* ---------------------------------------------------------------- Haru's logit shaping and DRY */
 
 /* DryConfig (haru/sampler.h:37-40, read by file_dry, haru/sampler.cpp:63-73). */

@@ -488,6 +488,69 @@ ssb_status ssb_sample_embed_rows(ssb_context * ctx, const ssb_rows * rows, const
     return ok();
 }
 
+int64_t ssb_shard_record_words(int32_t rows, int32_t k_cap) { return (int64_t) rows * ((int64_t) k_cap + 1); }
+
+static bool shard_kcap_ok(int32_t k_cap) { return k_cap >= 1 && k_cap <= ssb::kShardMaxK && (k_cap & (k_cap - 1)) == 0; }
+
+ssb_status ssb_shard_select(ssb_context * ctx, const ssb_rows * r, int32_t col_offset, int32_t vocab_total,
+                            int32_t k_cap, uint64_t * records, void * stream) {
+    if (!ctx || !r || !records) return fail(SSB_INVALID_ARGUMENT, "ctx, slice and records are required");
+    if (!shard_kcap_ok(k_cap)) return fail(SSB_INVALID_ARGUMENT, "k_cap must be a power of two in [1, 1024]");
+    if (col_offset < 0 || col_offset % 32 != 0) return fail(SSB_INVALID_ARGUMENT, "col_offset must be a non-negative multiple of 32");
+    if (r->vocab < 1 || (int64_t) col_offset + r->vocab > vocab_total || vocab_total > SSB_MAX_VOCAB)
+        return fail(SSB_INVALID_ARGUMENT, "the slice must lie inside [0, vocab_total)");
+    if (r->rows < 0 || r->ld < r->vocab) return fail(SSB_INVALID_ARGUMENT, "rows is negative or ld below the slice width");
+    if (r->dtype != SSB_F32 && r->dtype != SSB_BF16) return fail(SSB_INVALID_ARGUMENT, "dtype is neither SSB_F32 nor SSB_BF16");
+    if (r->mask_kind < SSB_MASK_NONE || r->mask_kind > SSB_MASK_ALLOW) return fail(SSB_INVALID_ARGUMENT, "mask_kind is not an ssb_mask_kind");
+    if (r->mask_kind != SSB_MASK_NONE && (!r->mask || (r->mask_ld > 0 && r->mask_ld < div_up(vocab_total, 32))))
+        return fail(SSB_INVALID_ARGUMENT, "the mask must hold ceil(vocab_total / 32) words per row");
+    if (r->history && (r->history_ld < 0 || r->history_ld > SSB_MAX_STREAM_HISTORY))
+        return fail(SSB_OUT_OF_RANGE, "history_ld must lie in [0, SSB_MAX_STREAM_HISTORY]");
+    if (r->rows == 0) return ok();
+    if (!r->logits) return fail(SSB_INVALID_ARGUMENT, "logits is null");
+    ssb_status st = use_device(ctx);
+    if (st != SSB_OK) return st;
+    ssb::ShardArgs a{};
+    a.r = rows_args(r, k_cap, nullptr);
+    a.r.mask = r->mask_kind != SSB_MASK_NONE ? r->mask + col_offset / 32 : nullptr;
+    a.col_offset = col_offset;
+    a.vocab_total = vocab_total;
+    a.k_cap = k_cap;
+    a.world = 1;
+    a.hist_slots = r->history ? ssb::next_pow2((int) std::max<int64_t>(4, 2 * r->history_ld)) : 0;
+    a.records = records;
+    if (ssb::shard_select_smem_bytes(k_cap, a.hist_slots) > (size_t) ctx->max_smem)
+        return fail(SSB_OUT_OF_RANGE, "k_cap and the history need more shared memory than the device has");
+    const cudaError_t e = ssb::launch_shard_select(a, r->dtype == SSB_BF16, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "shard select launch");
+    return ok();
+}
+
+ssb_status ssb_shard_merge(ssb_context * ctx, const ssb_rows * r, int32_t vocab_total, int32_t world, int32_t k_cap,
+                           const uint64_t * records, void * stream) {
+    if (!ctx || !r || !records) return fail(SSB_INVALID_ARGUMENT, "ctx, rows and records are required");
+    if (!shard_kcap_ok(k_cap)) return fail(SSB_INVALID_ARGUMENT, "k_cap must be a power of two in [1, 1024]");
+    if (world < 1 || world > 64) return fail(SSB_INVALID_ARGUMENT, "world must lie in [1, 64]");
+    if (vocab_total < 1 || vocab_total > SSB_MAX_VOCAB) return fail(SSB_INVALID_ARGUMENT, "vocab_total out of range");
+    if (r->rows < 0) return fail(SSB_INVALID_ARGUMENT, "rows is negative");
+    if (r->rows == 0) return ok();
+    if (!r->ids || !r->status) return fail(SSB_INVALID_ARGUMENT, "ids and status are required");
+    if (!(!r->row_params && r->params.greedy) && !r->u) return fail(SSB_INVALID_ARGUMENT, "u is required where a row draws (not greedy)");
+    if (ssb::shard_merge_smem_bytes(world, k_cap) > (size_t) ctx->max_smem)
+        return fail(SSB_OUT_OF_RANGE, "world x k_cap composites need more shared memory than the device has");
+    ssb_status st = use_device(ctx);
+    if (st != SSB_OK) return st;
+    ssb::ShardArgs a{};
+    a.r = rows_args(r, k_cap, nullptr);
+    a.vocab_total = vocab_total;
+    a.k_cap = k_cap;
+    a.world = world;
+    a.records = const_cast<uint64_t *>(records);
+    const cudaError_t e = ssb::launch_shard_merge(a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "shard merge launch");
+    return ok();
+}
+
 ssb_status ssb_lm_head_argmax(ssb_context * ctx, const ssb_lm_head * h, void * stream) {
     if (!ctx || !h) return fail(SSB_INVALID_ARGUMENT, "ctx and head are required");
     if (h->dtype != SSB_BF16) return fail(SSB_INVALID_ARGUMENT, "the LM head takes bf16 hidden rows and weights");

@@ -103,6 +103,23 @@ struct FlavorArgs {
 size_t flavor_smem_bytes(int cap, int bit_words, int hist_slots);
 cudaError_t launch_flavor(const FlavorArgs & a, bool bf16, bool debug, cudaStream_t stream);
 
+// The vocabulary-sharded draw (ssb_shard.cu): per slice, the k_cap best composites and (max, flags) of
+// each row as one record of k_cap + 1 words; after the all-gather, the merge of world records per row.
+struct ShardArgs {
+    RowsArgs r;        // select: the slice (vocab = width, mask at the slice's first word); merge: params, u, ids, status
+    int col_offset;    // the slice's first column (a multiple of 32)
+    int vocab_total;   // the whole row's width
+    int k_cap;         // composites per record (a power of two <= 1024)
+    int world;         // merge: records per row
+    int hist_slots;
+    uint64_t * records;  // select: [rows, k_cap + 1] out; merge: [world][rows][k_cap + 1] in
+};
+constexpr int kShardMaxK = 1024;
+size_t shard_select_smem_bytes(int k_cap, int hist_slots);
+size_t shard_merge_smem_bytes(int world, int k_cap);
+cudaError_t launch_shard_select(const ShardArgs & a, bool bf16, cudaStream_t stream);
+cudaError_t launch_shard_merge(const ShardArgs & a, cudaStream_t stream);
+
 // The LM head fused with its argmax (ssb_lmhead.cu): tcgen05 MMAs over 128-token tiles, the argmax in the
 // TMEM epilogue. n_pad = rows rounded up to 16 (the MMA's N); tmem_cols = two accumulators of n_pad.
 struct LmArgs {

@@ -93,6 +93,39 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False, 
     return lib
 
 
+NCCL_SRC = os.path.join(CSRC, "ssb_nccl.cpp")
+LIB_NCCL = os.path.join(PKG, "libspeech_sampler_b200_nccl.so")
+
+
+def nccl_dirs():
+    """(include, lib) of the NCCL that torch.distributed loads (the wheel's), else the system's."""
+    try:
+        import nvidia.nccl as n
+        base = os.path.dirname(n.__file__) if n.__file__ else list(n.__path__)[0]
+        inc, lib = os.path.join(base, "include"), os.path.join(base, "lib")
+        if os.path.exists(os.path.join(inc, "nccl.h")):
+            return inc, lib
+    except Exception:
+        pass
+    return "/usr/include", "/usr/lib/x86_64-linux-gnu"
+
+
+def build_nccl(force: bool = False, verbose: bool = False) -> str:
+    """libspeech_sampler_b200_nccl.so: the NCCL host code of the vocabulary-sharded draw, linked with the
+    engine (found next to it at run time) and libnccl.so.2."""
+    inc, libdir = nccl_dirs()
+    deps = [NCCL_SRC, LIB, os.path.join(INCLUDE, "speech_sampler_b200_nccl.h"), os.path.join(INCLUDE, "speech_sampler_b200.h")]
+    if not force and not _stale(LIB_NCCL, deps):
+        return LIB_NCCL
+    cmd = [nvcc()] + ARCH + ["-O2", "-std=c++17", "-shared", "-Xcompiler", "-fPIC", f"-I{INCLUDE}", f"-I{inc}", NCCL_SRC,
+           "-o", LIB_NCCL, f"-L{PKG}", "-lspeech_sampler_b200", f"-L{libdir}", "-l:libnccl.so.2",
+           "-Xlinker", "-rpath,$ORIGIN", "-Xlinker", f"-rpath,{libdir}"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    return LIB_NCCL
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
@@ -101,3 +134,4 @@ if __name__ == "__main__":
     args = ap.parse_args()
     print(build(force=args.force, verbose=args.verbose, ptxas_info=args.ptxas_info))
     print(build(force=args.force, verbose=args.verbose, waittest=True))
+    print(build_nccl(force=args.force, verbose=args.verbose))

@@ -146,6 +146,12 @@ def load_library(path: str = LIB_PATH):
     lib.ssb_sample_host.argtypes = [vp, ctypes.POINTER(Rows), vp]
     lib.ssb_restrict_rows.restype = ctypes.c_int
     lib.ssb_restrict_rows.argtypes = [vp, ctypes.POINTER(Rows), vp, ctypes.c_int64, vp]
+    lib.ssb_shard_record_words.restype = ctypes.c_int64
+    lib.ssb_shard_record_words.argtypes = [i32, i32]
+    lib.ssb_shard_select.restype = ctypes.c_int
+    lib.ssb_shard_select.argtypes = [vp, ctypes.POINTER(Rows), i32, i32, i32, vp, vp]
+    lib.ssb_shard_merge.restype = ctypes.c_int
+    lib.ssb_shard_merge.argtypes = [vp, ctypes.POINTER(Rows), i32, i32, i32, vp, vp]
     lib.ssb_lm_head_argmax.restype = ctypes.c_int
     lib.ssb_lm_head_argmax.argtypes = [vp, ctypes.POINTER(LmHead), vp]
     lib.ssb_sample_embed_rows.restype = ctypes.c_int
@@ -278,6 +284,32 @@ class Sampler:
         e.out_ld = out.stride(0)
         s = None if stream is None else ctypes.c_void_p(stream.cuda_stream)
         _check(self.lib, self.lib.ssb_sample_embed_rows(self.ctx, ctypes.byref(r), ctypes.byref(e), s))
+        return ids, status
+
+    def shard_select(self, logits_slice, p, col_offset: int, vocab_total: int, k_cap: int, records, history=None,
+                     history_len=None, mask=None, mask_kind=MASK_NONE, row_params=None, stream=None):
+        """Step 1 of the vocabulary-sharded draw on this slice (history: the rows' global ids; mask: the
+        whole rows' words); records: uint64 device tensor of ssb_shard_record_words(rows, k_cap) words."""
+        r = self._rows_struct(logits_slice, p, history, history_len, mask, mask_kind, None, None, None, row_params)
+        s = None if stream is None else ctypes.c_void_p(stream.cuda_stream)
+        _check(self.lib, self.lib.ssb_shard_select(self.ctx, ctypes.byref(r), col_offset, vocab_total, k_cap,
+                                                  _dptr(records), s))
+
+    def shard_merge(self, rows: int, p, vocab_total: int, world: int, k_cap: int, records, u=None, row_params=None,
+                    ids=None, status=None, stream=None):
+        """Step 2: ids and statuses of `rows` rows from the world ranks' records ([world][rows][k_cap + 1])."""
+        import torch
+        dev = records.device
+        ids = torch.empty(rows, dtype=torch.int32, device=dev) if ids is None else ids
+        status = torch.empty(rows, dtype=torch.int32, device=dev) if status is None else status
+        r = Rows()
+        r.rows, r.vocab, r.ld, r.dtype = rows, vocab_total, vocab_total, F32
+        r.params = p if p is not None else params()
+        r.row_params = _dptr(row_params)
+        r.u, r.ids, r.status = _dptr(u), _dptr(ids), _dptr(status)
+        s = None if stream is None else ctypes.c_void_p(stream.cuda_stream)
+        _check(self.lib, self.lib.ssb_shard_merge(self.ctx, ctypes.byref(r), vocab_total, world, k_cap,
+                                                 _dptr(records), s))
         return ids, status
 
     def lm_head_argmax(self, hidden, weight, ids=None, max_logit=None, status=None, stream=None):

@@ -20,6 +20,8 @@ mask. The exchange is 4 bytes per column of the row; at B = 1 the step is latenc
 """
 from __future__ import annotations
 
+import os
+
 import speech_sampler as ss
 
 
@@ -107,8 +109,104 @@ def sample_slices_on_one_device(sampler, logits, world: int, p, history=None, ma
     return sample_whole(sampler, assemble(slices, bounds, vocab), p, u)
 
 
+# ---------------------------------------------------------------- the candidate exchange (top-k rows)
+# Rows whose effective top-k is at most k_cap (and greedy rows) need only each slice's k_cap best
+# composites: ssb_shard_select on every rank, one all-gather of rows * (k_cap + 1) words per rank,
+# ssb_shard_merge on every rank (speech.cpp_b200/csrc/ssb_shard.cu). Over NCCL the C++ library
+# libspeech_sampler_b200_nccl.so runs the three steps on one stream (ShardComm.sample).
+
+def records_tensor(rows: int, k_cap: int, world: int = 1, device="cuda"):
+    import torch
+    lib = ss.load_library()
+    return torch.empty((world, lib.ssb_shard_record_words(rows, k_cap)), dtype=torch.int64, device=device)
+
+
+def sample_topk_on_one_device(sampler, logits, world: int, p, history=None, mask=None, mask_kind=ss.MASK_NONE,
+                              u=None, k_cap: int = 64, row_params=None):
+    """The candidate exchange with `world` slices of each row selected one after another on one device into
+    the gathered layout (no collective): the single-GPU check of the protocol. Returns (ids, status)."""
+    rows, vocab = logits.shape
+    rec = records_tensor(rows, k_cap, world, logits.device)
+    for rank, (off, width) in enumerate(shard_bounds(vocab, world)):
+        sampler.shard_select(logits[:, off:off + width], p, off, vocab, k_cap, rec[rank], history, None, mask,
+                             mask_kind, row_params)
+    return sampler.shard_merge(rows, p, vocab, world, k_cap, rec, u, row_params)
+
+
+NCCL_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(ss.__file__)), "libspeech_sampler_b200_nccl.so")
+
+
+def load_nccl_library(path: str = NCCL_LIB_PATH):
+    """The NCCL host library of the exchange (include/speech_sampler_b200_nccl.h). Raises if not built."""
+    import ctypes
+    if not os.path.exists(path):
+        raise FileNotFoundError(f"{path} is not built: run python speech.cpp_b200/speech_build.py")
+    ss.load_library()
+    lib = ctypes.CDLL(path)
+    vp, i32 = ctypes.c_void_p, ctypes.c_int32
+    lib.ssb_nccl_unique_id.restype = ctypes.c_int
+    lib.ssb_nccl_unique_id.argtypes = [vp]
+    lib.ssb_shard_comm_create.restype = ctypes.c_int
+    lib.ssb_shard_comm_create.argtypes = [vp, vp, i32, i32, ctypes.POINTER(vp)]
+    lib.ssb_shard_comm_destroy.restype = ctypes.c_int
+    lib.ssb_shard_comm_destroy.argtypes = [vp]
+    lib.ssb_shard_comm_reserve.restype = ctypes.c_int
+    lib.ssb_shard_comm_reserve.argtypes = [vp, i32, i32]
+    lib.ssb_shard_sample.restype = ctypes.c_int
+    lib.ssb_shard_sample.argtypes = [vp, ctypes.POINTER(ss.Rows), i32, i32, i32, vp]
+    lib.ssb_nccl_last_error.restype = ctypes.c_char_p
+    return lib
+
+
+class ShardComm:
+    """An NCCL communicator of the exchange over the ranks of a torch.distributed group (the unique id
+    travels by the group's broadcast)."""
+
+    def __init__(self, sampler, group=None):
+        import ctypes
+        import torch
+        import torch.distributed as dist
+        self.lib = load_nccl_library()
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        uid = (ctypes.c_uint8 * 128)()
+        if self.rank == 0:
+            self._check(self.lib.ssb_nccl_unique_id(uid))
+        t = torch.tensor(list(bytes(uid)), dtype=torch.uint8, device="cuda")
+        dist.broadcast(t, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+        uid = (ctypes.c_uint8 * 128)(*t.cpu().tolist())
+        h = ctypes.c_void_p()
+        self._check(self.lib.ssb_shard_comm_create(sampler.ctx, uid, self.world, self.rank, ctypes.byref(h)))
+        self.h = h
+
+    def _check(self, status):
+        if status != ss.OK:
+            raise ss.SsbError(status, self.lib.ssb_nccl_last_error().decode())
+
+    def reserve(self, rows: int, k_cap: int):
+        self._check(self.lib.ssb_shard_comm_reserve(self.h, rows, k_cap))
+
+    def sample(self, logits_slice, p, col_offset: int, vocab_total: int, k_cap: int, history=None, mask=None,
+               mask_kind=ss.MASK_NONE, u=None, row_params=None, ids=None, status=None, stream=None):
+        """The sharded draw of this rank's slice (collective). Returns (ids, status), equal on every rank."""
+        import ctypes
+        import torch
+        rows = logits_slice.shape[0]
+        ids = torch.empty(rows, dtype=torch.int32, device=logits_slice.device) if ids is None else ids
+        status = torch.empty(rows, dtype=torch.int32, device=logits_slice.device) if status is None else status
+        r = ss.Sampler._rows_struct(logits_slice, p, history, None, mask, mask_kind, u, ids, status, row_params)
+        s = None if stream is None else ctypes.c_void_p(stream.cuda_stream)
+        self._check(self.lib.ssb_shard_sample(self.h, ctypes.byref(r), col_offset, vocab_total, k_cap, s))
+        return ids, status
+
+    def close(self):
+        if self.h:
+            self.lib.ssb_shard_comm_destroy(self.h)
+            self.h = None
+
+
 __all__ = ["shard_bounds", "local_history", "local_mask", "restrict_slice", "assemble", "sample_whole",
-           "sample_vocab_sharded", "sample_slices_on_one_device"]
+           "sample_vocab_sharded", "sample_slices_on_one_device", "records_tensor", "sample_topk_on_one_device",
+           "load_nccl_library", "ShardComm"]
 
 
 def _main():
@@ -161,5 +259,66 @@ def _main():
         dist.destroy_process_group()
 
 
+def _main_topk():
+    """Under torchrun (one rank per GPU, NCCL): config 4's 64-row batches (bf16, history, penalties, top-k 40)
+    sampled with the candidate exchange over NCCL (ShardComm: select, one ncclAllGather, merge, on one
+    stream), every rank's ids checked against the whole-row engine on its own GPU, and the exchange timed
+    (CUDA events, max over ranks) beside the restricted-slice exchange of the same rows. Rank 0 prints one
+    JSON line.
+        python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 \
+            speech.cpp_b200/speech_vocab_shard.py --protocol topk
+    """
+    import json
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import speech_workloads as wl
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    rank, world = dist.get_rank(), dist.get_world_size()
+    sampler = ss.Sampler(local)
+    comm = ShardComm(sampler)
+    try:
+        rows, k_cap = 64, 64
+        c = wl.config4(rows=rows)
+        x = torch.from_numpy(c["logits_bf16"]).view(torch.bfloat16).cuda()
+        h = torch.from_numpy(c["history"]).cuda()
+        u = torch.from_numpy(c["u"]).cuda()
+        p = ss.params(**c["params"])
+        vocab = x.shape[1]
+        off, width = shard_bounds(vocab, world)[rank]
+        sl = x[:, off:off + width]
+        comm.reserve(rows, k_cap)
+        ids_w, st_w = sampler.sample(x, p, h, u=u)
+        stream = torch.cuda.current_stream()
+        times = []
+        for rep in range(25):
+            dist.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            e0.record(stream)
+            ids_s, st_s = comm.sample(sl, p, off, vocab, k_cap, history=h, u=u, stream=stream)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            if rep >= 5:
+                times.append(e0.elapsed_time(e1) * 1e3)
+        equal = bool(torch.equal(ids_w, ids_s) and torch.equal(st_w, st_s))
+        t = torch.tensor([float(np.median(times)), 0.0 if equal else 1.0], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        if rank == 0:
+            print(json.dumps({"vocab_sharded": "candidate exchange (NCCL)", "ranks": world, "vocab": vocab,
+                              "rows": rows, "k_cap": k_cap, "us_per_batch_max_over_ranks": float(t[0]),
+                              "ids_equal_whole_row": bool(t[1] == 0)}))
+    finally:
+        comm.close()
+        sampler.close()
+        dist.destroy_process_group()
+
+
 if __name__ == "__main__":
-    _main()
+    import sys
+    if "--protocol" in sys.argv and sys.argv[sys.argv.index("--protocol") + 1] == "topk":
+        _main_topk()
+    else:
+        _main()

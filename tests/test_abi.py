@@ -98,3 +98,17 @@ def test_no_device_fails_loudly(lib):
     assert st in (ss.DEVICE, ss.INVALID_ARGUMENT) and not ctx.value
     with pytest.raises(ss.SsbError):
         ss.Sampler(0)
+
+
+def test_nccl_library_exports():
+    """The NCCL host library of the vocabulary-sharded draw loads (with the engine and libnccl) and exports
+    every function its header declares."""
+    import os
+    import re
+    import speech_vocab_shard as vs
+    lib = vs.load_nccl_library()
+    header = os.path.join(os.path.dirname(ss.HEADER), "speech_sampler_b200_nccl.h")
+    names = re.findall(r"SSB_API\s+[^;(]*?\b(ssb_\w+)\s*\(", open(header).read())
+    assert len(names) == 6
+    for n in names:
+        assert hasattr(lib, n), n

@@ -71,3 +71,71 @@ def test_statuses_decided_on_the_whole_row(engine):
         whole, sliced = whole_and_sliced(engine, dev(row), 4, p, mask=m,
                                          mask_kind=ss.MASK_BAN if mask is not None else ss.MASK_NONE, u=u)
         assert whole == sliced and whole[1] == want
+
+
+# ---------------------------------------------------------------- the candidate exchange (top-k rows)
+def _exchange_vs_whole(engine, x, world, p, k_cap, history=None, mask=None, mask_kind=ss.MASK_NONE, u=None,
+                       row_params=None, max_top_k=0):
+    import torch
+    ids_w, st_w = engine.sample(x, p, history, None, mask, mask_kind, u, row_params, max_top_k)
+    ids_s, st_s = vs.sample_topk_on_one_device(engine, x, world, p, history, mask, mask_kind, u, k_cap, row_params)
+    torch.cuda.synchronize()
+    return ids_w.cpu().numpy(), st_w.cpu().numpy(), ids_s.cpu().numpy(), st_s.cpu().numpy()
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_exchange_config4_batch(engine, world):
+    """Config 4's rows (bf16, 1024 history ids, repetition/presence/frequency penalties, top-k 40, top-p
+    0.95) as `world` slices: each slice's 64 best composites, merged: ids and statuses equal the
+    whole-row engine's on all 64 rows."""
+    c = wl.config4(rows=64)
+    import torch
+    x = dev(c["logits_bf16"], torch.bfloat16)
+    p = ss.params(**c["params"])
+    iw, sw, i_s, s_s = _exchange_vs_whole(engine, x, world, p, 64, dev(c["history"]), u=dev(c["u"]))
+    assert np.array_equal(sw, s_s) and np.all(sw == ss.ROW_OK)
+    assert np.array_equal(iw, i_s)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_exchange_talker_and_greedy_masked(engine, world):
+    """Talker rows (3072 codes, k 50, penalty 1.05 over 512 ids) and greedy rows with a ban mask (the ASR
+    suppress mask at 151936 tokens), k_cap 64 and 1."""
+    import torch
+    t = wl.config2(steps=16)
+    p2 = ss.params(**t["params"])
+    iw, sw, i_s, s_s = _exchange_vs_whole(engine, dev(t["logits"]), world, p2, 64, dev(t["history"]), u=dev(t["u"]))
+    assert np.array_equal(sw, s_s) and np.array_equal(iw, i_s)
+    c1 = wl.config1(rows=8)
+    m = dev(c1["mask"].view(np.int32))
+    iw, sw, i_s, s_s = _exchange_vs_whole(engine, dev(c1["logits"]), world, ss.params(greedy=True), 1, mask=m,
+                                          mask_kind=ss.MASK_BAN)
+    assert np.array_equal(sw, s_s) and np.array_equal(iw, i_s)
+
+
+def test_exchange_statuses_and_row_params(engine):
+    """NaN, +inf with a penalty, every token banned, an overflowing temperature, a greedy row and a row
+    keeping more than k_cap (top-k 0: INVALID_ROW) among per-row settings."""
+    import torch
+    rng = np.random.default_rng(17)
+    V = 20000
+    x = (rng.standard_normal((6, V)) * 2).astype(np.float32)
+    x[0, 1234] = np.nan
+    x[1, 50] = np.inf
+    x[3, :] *= np.float32(1e30)
+    hist = np.full((6, 4), -1, np.int32)
+    hist[1, 0] = 50
+    ban = np.zeros((6, V), bool)
+    ban[2, :] = True
+    mask = wl.pack_mask(ban)
+    plist = [ss.params(temperature=0.9, top_k=40), ss.params(temperature=0.9, top_k=40, repetition_penalty=1.3),
+             ss.params(temperature=0.9, top_k=40), ss.params(temperature=1e-30, top_k=40),
+             ss.params(greedy=True, repetition_penalty=1.3), ss.params(temperature=0.9, top_k=0)]
+    u = rng.random(6)
+    rp = dev(ss.params_array(plist).view(np.uint8)).view(torch.int32)
+    iw, sw, i_s, s_s = _exchange_vs_whole(engine, dev(x), 4, plist[0], 64, dev(hist), dev(mask.view(np.int32)),
+                                          ss.MASK_BAN, dev(u), rp, max_top_k=0)
+    assert list(s_s[:5]) == list(sw[:5]) == [ss.ROW_NON_FINITE_INPUT, ss.ROW_PENALTY_OVERFLOW, ss.ROW_NO_FINITE_LOGIT,
+                                             ss.ROW_TEMPERATURE_OVERFLOW, ss.ROW_OK]
+    assert i_s[4] == iw[4]
+    assert s_s[5] == ss.ROW_INVALID_ROW and i_s[5] == -1
