@@ -519,8 +519,11 @@ ssb_status ssb_shard_select(ssb_context * ctx, const ssb_rows * r, int32_t col_o
     a.world = 1;
     a.hist_slots = r->history ? ssb::next_pow2((int) std::max<int64_t>(4, 2 * r->history_ld)) : 0;
     a.records = records;
-    if (ssb::shard_select_smem_bytes(k_cap, a.hist_slots) > (size_t) ctx->max_smem)
-        return fail(SSB_OUT_OF_RANGE, "k_cap and the history need more shared memory than the device has");
+    const int words = (int) div_up(r->vocab, 32);
+    a.bit_words = r->history && words <= 8192 ? words : 0;  // the bitmap where it fits in 32 KB
+    if (ssb::shard_select_smem_bytes(a.bit_words, a.hist_slots) > (size_t) ctx->max_smem) a.bit_words = 0;
+    if (ssb::shard_select_smem_bytes(a.bit_words, a.hist_slots) > (size_t) ctx->max_smem)
+        return fail(SSB_OUT_OF_RANGE, "the history needs more shared memory than the device has");
     const cudaError_t e = ssb::launch_shard_select(a, r->dtype == SSB_BF16, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "shard select launch");
     return ok();

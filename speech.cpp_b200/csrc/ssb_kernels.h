@@ -112,10 +112,11 @@ struct ShardArgs {
     int k_cap;         // composites per record (a power of two <= 1024)
     int world;         // merge: records per row
     int hist_slots;
+    int bit_words;       // select: words of the history-column bitmap (ceil(width / 32)), or 0
     uint64_t * records;  // select: [rows, k_cap + 1] out; merge: [world][rows][k_cap + 1] in
 };
 constexpr int kShardMaxK = 1024;
-size_t shard_select_smem_bytes(int k_cap, int hist_slots);
+size_t shard_select_smem_bytes(int bit_words, int hist_slots);
 size_t shard_merge_smem_bytes(int world, int k_cap);
 cudaError_t launch_shard_select(const ShardArgs & a, bool bf16, cudaStream_t stream);
 cudaError_t launch_shard_merge(const ShardArgs & a, cudaStream_t stream);

@@ -260,7 +260,8 @@ def _main():
 
 
 def _main_topk():
-    """Under torchrun (one rank per GPU, NCCL): config 4's 64-row batches (bf16, history, penalties, top-k 40)
+    """Under torchrun (one rank per GPU, NCCL): config 4's rows, one row and a 64-row batch (bf16, history,
+    penalties, top-k 40)
     sampled with the candidate exchange over NCCL (ShardComm: select, one ncclAllGather, merge, on one
     stream), every rank's ids checked against the whole-row engine on its own GPU, and the exchange timed
     (CUDA events, max over ranks) beside the restricted-slice exchange of the same rows. Rank 0 prints one
@@ -280,36 +281,40 @@ def _main_topk():
     sampler = ss.Sampler(local)
     comm = ShardComm(sampler)
     try:
-        rows, k_cap = 64, 64
-        c = wl.config4(rows=rows)
-        x = torch.from_numpy(c["logits_bf16"]).view(torch.bfloat16).cuda()
-        h = torch.from_numpy(c["history"]).cuda()
-        u = torch.from_numpy(c["u"]).cuda()
+        k_cap = 64
+        c = wl.config4(rows=64)
         p = ss.params(**c["params"])
-        vocab = x.shape[1]
-        off, width = shard_bounds(vocab, world)[rank]
-        sl = x[:, off:off + width]
-        comm.reserve(rows, k_cap)
-        ids_w, st_w = sampler.sample(x, p, h, u=u)
-        stream = torch.cuda.current_stream()
-        times = []
-        for rep in range(25):
-            dist.barrier()
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
-            e0.record(stream)
-            ids_s, st_s = comm.sample(sl, p, off, vocab, k_cap, history=h, u=u, stream=stream)
-            e1.record(stream)
-            torch.cuda.synchronize()
-            if rep >= 5:
-                times.append(e0.elapsed_time(e1) * 1e3)
-        equal = bool(torch.equal(ids_w, ids_s) and torch.equal(st_w, st_s))
-        t = torch.tensor([float(np.median(times)), 0.0 if equal else 1.0], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        out = {}
+        for rows in (1, 64):
+            x = torch.from_numpy(c["logits_bf16"][:rows]).view(torch.bfloat16).cuda()
+            h = torch.from_numpy(c["history"][:rows]).cuda()
+            u = torch.from_numpy(c["u"][:rows]).cuda()
+            vocab = x.shape[1]
+            off, width = shard_bounds(vocab, world)[rank]
+            sl = x[:, off:off + width]
+            comm.reserve(rows, k_cap)
+            ids_w, st_w = sampler.sample(x, p, h, u=u)
+            stream = torch.cuda.current_stream()
+            times = []
+            for rep in range(25):
+                dist.barrier()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+                e0.record(stream)
+                ids_s, st_s = comm.sample(sl, p, off, vocab, k_cap, history=h, u=u, stream=stream)
+                e1.record(stream)
+                torch.cuda.synchronize()
+                if rep >= 5:
+                    times.append(e0.elapsed_time(e1) * 1e3)
+            equal = bool(torch.equal(ids_w, ids_s) and torch.equal(st_w, st_s))
+            t = torch.tensor([float(np.median(times)), 0.0 if equal else 1.0], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            out[rows] = (float(t[0]), bool(t[1] == 0))
         if rank == 0:
             print(json.dumps({"vocab_sharded": "candidate exchange (NCCL)", "ranks": world, "vocab": vocab,
-                              "rows": rows, "k_cap": k_cap, "us_per_batch_max_over_ranks": float(t[0]),
-                              "ids_equal_whole_row": bool(t[1] == 0)}))
+                              "k_cap": k_cap, "workload": "config 4 rows (bf16, 1024 history ids, top-k 40)",
+                              "us_per_call_max_over_ranks": {str(r): v[0] for r, v in out.items()},
+                              "ids_equal_whole_row": all(v[1] for v in out.values())}))
     finally:
         comm.close()
         sampler.close()
