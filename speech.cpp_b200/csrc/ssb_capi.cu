@@ -6,6 +6,8 @@
 #include <cstdint>
 #include <cstring>
 #include <string>
+#include <map>
+#include <mutex>
 #include <thread>
 #include <vector>
 
@@ -52,6 +54,24 @@ struct ssb_dry {
     void * block = nullptr;
     ssb::DryArgs a{};
 };
+
+namespace ssb {
+
+cudaError_t set_max_dynamic_smem(const void * kernel, size_t bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<int, const void *>, size_t> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(mu);
+    size_t & have = done[{dev, kernel}];
+    if (bytes <= have) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) bytes);
+    if (e == cudaSuccess) have = bytes;
+    return e;
+}
+
+}  // namespace ssb
 
 namespace {
 
@@ -265,6 +285,27 @@ ssb_status run(ssb_context * ctx, const ssb_rows * r, const Debug * dbg, cudaStr
     sa.hist_slots = r->history ? ssb::next_pow2((int) std::max<int64_t>(4, 2 * r->history_ld)) : 0;  // hash, load <= 1/2
     sa.cap = mode == 1 ? (int) div_up(kb + std::max(1024, kb), 32) * 32 : 0;
     sa.sel_slots = mode == 1 ? ssb::next_pow2(std::max(kb, 2)) : 0;
+    // all-greedy batches on aligned rows: the split-row argmax (not for the candidate export, which also
+    // wants every restricted logit)
+    if (mode == 0 && vec && !debug) {
+        const int unit = ssb::argmax_unit(bf16);
+        const int64_t units = div_up(r->vocab, unit);
+        const int64_t per_row = std::max<int64_t>(1, ctx->max_slots / std::max(1, r->rows));
+        const int64_t splits = std::min<int64_t>(units, per_row);
+        const int64_t chunk = div_up(units, splits) * unit;
+        sa.splits = (int) div_up(r->vocab, chunk);
+        sa.chunk = (int) chunk;
+        if (ssb::argmax_smem_bytes(sa.chunk, sa.hist_slots) <= (size_t) ctx->max_smem) {
+            if (sa.splits > 1) {
+                sa.part_cand = ctx->part_cand;
+                sa.part_max = ctx->part_max;
+                sa.counters = ctx->counters;
+            }
+            e = ssb::launch_argmax(sa, bf16, stream);
+            if (e != cudaSuccess) return cuda_fail(e, "argmax kernel launch");
+            return ok();
+        }
+    }
     // aligned rows with a small top-k (or all greedy: top-1) take the warp-specialized top-k kernel
     bool use_topk = vec && (mode == 0 || kb <= ssb::kTopkMaxK);
     const int kw = use_topk ? ssb::topk_kw(kb) : -1;

@@ -389,7 +389,7 @@ __global__ void __launch_bounds__(kFlThreads) flavor_rows_kernel(const __grid_co
 template <typename TIn, bool kDebug>
 cudaError_t launch_t(const FlavorArgs & a, size_t smem, cudaStream_t stream) {
     auto kern = flavor_rows_kernel<TIn, kDebug>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    cudaError_t e = ssb::set_max_dynamic_smem((const void *) kern, smem);
     if (e != cudaSuccess) return e;
     kern<<<a.r.rows, kFlThreads, smem, stream>>>(a);
     return cudaGetLastError();

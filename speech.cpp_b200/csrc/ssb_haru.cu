@@ -156,7 +156,7 @@ size_t dry_smem_bytes(int window) { return (size_t) next_pow2(window) * 8 + (siz
 
 cudaError_t launch_dry_update(const DryArgs & a, const int32_t * tokens, cudaStream_t stream) {
     const size_t smem = dry_smem_bytes(a.window);
-    cudaError_t e = cudaFuncSetAttribute(dry_update_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    cudaError_t e = ssb::set_max_dynamic_smem((const void *) dry_update_kernel, smem);
     if (e != cudaSuccess) return e;
     dry_update_kernel<<<a.streams, kDryThreads, smem, stream>>>(a, tokens);
     return cudaGetLastError();

@@ -9,6 +9,10 @@
 
 namespace ssb {
 
+// cudaFuncSetAttribute(kernel, MaxDynamicSharedMemorySize, bytes) once per (device, kernel) and size:
+// a launch that needs no more than the kernel already allows costs no attribute call (ssb_capi.cu).
+cudaError_t set_max_dynamic_smem(const void * kernel, size_t bytes);
+
 // Fields every kernel reads: the batch (device pointers) plus the optional parity/debug outputs.
 struct RowsArgs {
     const void * logits;
@@ -64,6 +68,12 @@ cudaError_t launch_small(const SmallArgs & a, bool bf16, bool debug, cudaStream_
 size_t stream_smem_bytes(int mode, bool vec, int chunk, int hist_slots, int cap, int sel_slots);
 cudaError_t launch_stream(const StreamArgs & a, int mode, bool bf16, bool vec, bool debug, cudaStream_t stream);
 int stream_blocks_per_sm(int mode, bool bf16, bool vec, size_t smem);
+
+// All-greedy batches on aligned rows (ssb_argmax.cu): grid (splits, rows), chunks a multiple of
+// argmax_unit columns (one 16-byte load per thread), partial maxima merged by the row's last CTA.
+int argmax_unit(bool bf16);
+size_t argmax_smem_bytes(int chunk, int hist_slots);
+cudaError_t launch_argmax(const StreamArgs & a, bool bf16, cudaStream_t stream);
 
 // Top-k kernel (ssb_topk.cu) for 16-byte-aligned rows with top-k <= kTopkMaxK, greedy rows as the
 // top-1 of their unscaled logits: kw = the width of its warp lists in registers (1, 2 or 4: top-k up

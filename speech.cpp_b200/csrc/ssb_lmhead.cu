@@ -322,7 +322,7 @@ cudaError_t launch_lm_argmax(const LmArgs & a, const void * hidden, int64_t hidd
         !make_map(&mh, hidden, a.rows, a.dim, hidden_ld, a.n_pad))
         return cudaErrorInvalidValue;
     const size_t smem = lm_smem_bytes(a.n_pad, a.stages);
-    cudaError_t e = cudaFuncSetAttribute(lm_argmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    cudaError_t e = ssb::set_max_dynamic_smem((const void *) lm_argmax_kernel, smem);
     if (e != cudaSuccess) return e;
     lm_argmax_kernel<<<grid, kLmThreads, smem, stream>>>(mw, mh, a);
     e = cudaGetLastError();

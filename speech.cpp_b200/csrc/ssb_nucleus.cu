@@ -638,7 +638,7 @@ int nucleus_threads() { return kNThreads; }
 
 int nucleus_blocks_per_sm(bool bf16, size_t smem) {
     void * kern = pick_kernel(bf16, false);
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem) != cudaSuccess) return 0;
+    if (ssb::set_max_dynamic_smem((const void *) kern, smem) != cudaSuccess) return 0;
     int n = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kNThreads, smem) != cudaSuccess) return 0;
     return n;
@@ -647,7 +647,7 @@ int nucleus_blocks_per_sm(bool bf16, size_t smem) {
 cudaError_t launch_nucleus(const NucleusArgs & a, int grid, bool bf16, bool debug, cudaStream_t stream) {
     const size_t smem = nucleus_smem_bytes(a.r.vocab, a.hist_slots);
     void * kern = pick_kernel(bf16, debug);
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    cudaError_t e = ssb::set_max_dynamic_smem((const void *) kern, smem);
     if (e != cudaSuccess) return e;
     void * args[] = {const_cast<NucleusArgs *>(&a)};
     return cudaLaunchKernel(kern, dim3((unsigned) grid), dim3(kNThreads), args, smem, stream);

@@ -92,7 +92,7 @@ cudaError_t launch_restrict(const RowsArgs & a, int hist_slots, bool bf16, float
     const size_t smem = restrict_smem_bytes(hist_slots);
     void * kern = bf16 ? reinterpret_cast<void *>(restrict_history_kernel<uint16_t>)
                        : reinterpret_cast<void *>(restrict_history_kernel<float>);
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    e = ssb::set_max_dynamic_smem((const void *) kern, smem);
     if (e != cudaSuccess) return e;
     const int blocks = std::min(a.rows, 4 * sm_count);
     if (bf16) restrict_history_kernel<uint16_t><<<blocks, kRestrictThreads, smem, stream>>>(a, hist_slots, out, out_ld);

@@ -7,8 +7,10 @@
 //                        and the slice's k best composites (scaled logit, or the restricted logit for a
 //                        greedy row, with the token's GLOBAL index), sorted, into one record per row:
 //                        k_cap composites (0 = none) and a word (max bits << 32 | flags). Two passes over
-//                        the slice: a 4096-bin histogram of the keys' top 12 bits gives the bin of the k-th
-//                        key; the keys at or above it (at most 4096, else a radix select) are sorted.
+//                        the slice with eight loads in flight per thread and no atomics on the bulk: each
+//                        thread's two best composites give a floor (the k-th largest of them, below which
+//                        none of the k best lies); the composites at or above it (a few times k, at most
+//                        4096, else a radix select) are sorted.
 //   (the records of all ranks are all-gathered: one collective of rows * (k_cap + 1) * 8 bytes per rank)
 //   shard_merge_kernel   (every rank, identically) per row: the global maximum and flags give the row's
 //                        status exactly as the whole-row kernels decide it (restricted_status, then a NaN
@@ -31,8 +33,7 @@ namespace {
 
 constexpr int kShardThreads = 512;
 constexpr int kShardUnroll = 8;  // logits loads in flight per thread in the passes over the slice
-constexpr int kShardBins = 4096;  // histogram of the top 12 bits of the keys
-constexpr int kShardList = 4096;  // candidates kept for the exact sort (>= k_cap)
+constexpr int kShardList = 4096;  // candidates kept for the exact sort (>= 2 x threads >= k_cap)
 
 __device__ __forceinline__ int sh_find(const int32_t * keys, int slots, int bits, int32_t t) {
     const uint32_t mask = (uint32_t) slots - 1u;
@@ -46,20 +47,18 @@ __device__ __forceinline__ int sh_find(const int32_t * keys, int slots, int bits
     return -1;
 }
 
-template <typename TIn>
+template <typename TIn, bool kVecLoad>
 __global__ void __launch_bounds__(kShardThreads) shard_select_kernel(const __grid_constant__ ShardArgs sa) {
     const RowsArgs & a = sa.r;
     extern __shared__ __align__(16) unsigned char smem[];
     uint64_t * s_list = reinterpret_cast<uint64_t *>(smem);                 // [kShardList] candidates
-    uint32_t * s_hist = reinterpret_cast<uint32_t *>(s_list + kShardList);  // [kShardBins]
-    uint32_t * s_bits = s_hist + kShardBins;                                // [bit_words] history columns
+    uint32_t * s_bits = reinterpret_cast<uint32_t *>(s_list + kShardList);  // [bit_words] history columns
     int32_t * s_hkey = reinterpret_cast<int32_t *>(s_bits + sa.bit_words);  // [hist_slots]
     int32_t * s_hcnt = s_hkey + sa.hist_slots;
     __shared__ SelectState sel;
     __shared__ float s_redf[32];
     __shared__ int s_redi[32];
-    __shared__ uint32_t s_scan[kShardThreads];
-    __shared__ int s_n, s_bin;
+    __shared__ int s_n;
 
     const int row = blockIdx.x, tid = (int) threadIdx.x, lane = lane_id();
     const int width = a.vocab;
@@ -83,7 +82,6 @@ __global__ void __launch_bounds__(kShardThreads) shard_select_kernel(const __gri
     const bool use_bits = penal && sa.bit_words >= ((width + 31) >> 5);
 
     // the history ids inside the slice, as slice columns, with their counts, and a bitmap of them
-    for (int i = tid; i < kShardBins; i += kShardThreads) s_hist[i] = 0u;
     if (penal) {
         for (int i = tid; i < slots; i += kShardThreads) s_hkey[i] = -1, s_hcnt[i] = 0;
         if (use_bits)
@@ -119,94 +117,133 @@ __global__ void __launch_bounds__(kShardThreads) shard_select_kernel(const __gri
         return composite(greedy ? r : __fdiv_rn(r, p.temperature), (uint32_t) (sa.col_offset + col));
     };
     auto key_of = [&](int col) { return key_from(restricted(col), col); };
-    // kShardUnroll columns per thread and step (col = base + j * threads + tid), their loads issued together
-    auto load_step = [&](int base, float (&v)[kShardUnroll]) {
+    // kPerStep columns per thread and step, their loads issued together: kShardUnroll scalar loads
+    // (column base + j * threads + tid), or on 16-byte-aligned slices kShardUnroll / 2 vector loads of
+    // Elem::kVec columns each (column base + (j * threads + tid) * kVec + e)
+    constexpr int kVecN = kVecLoad ? Elem<TIn>::kVec : 1;
+    constexpr int kLoads = kVecLoad ? kShardUnroll / 2 : kShardUnroll;
+    constexpr int kPerStep = kLoads * kVecN;
+    auto col_of = [&](int base, int i) {  // the column of the thread's i-th value of a step
+        return kVecLoad ? base + ((i / kVecN) * kShardThreads + tid) * kVecN + (i % kVecN) : base + i * kShardThreads + tid;
+    };
+    auto load_step = [&](int base, float (&v)[kPerStep]) {
+        if constexpr (kVecLoad) {
 #pragma unroll
-        for (int j = 0; j < kShardUnroll; j++) {
-            const int col = base + j * kShardThreads + tid;
-            v[j] = col < width ? Elem<TIn>::load1(src, col) : 0.0f;
+            for (int j = 0; j < kLoads; j++) {
+                const int c = base + (j * kShardThreads + tid) * kVecN;
+                if (c + kVecN <= width) {
+                    float u[kVecN];
+                    Elem<TIn>::unpack(ld_stream(src + c), u);
+#pragma unroll
+                    for (int e = 0; e < kVecN; e++) v[j * kVecN + e] = u[e];
+                } else {
+#pragma unroll
+                    for (int e = 0; e < kVecN; e++) v[j * kVecN + e] = c + e < width ? Elem<TIn>::load1(src, c + e) : 0.0f;
+                }
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < kPerStep; j++) {
+                const int col = base + j * kShardThreads + tid;
+                v[j] = col < width ? Elem<TIn>::load1(src, col) : 0.0f;
+            }
         }
     };
-    constexpr int kStep = kShardUnroll * kShardThreads;
+    constexpr int kStep = kPerStep * kShardThreads;
 
-    // pass 1: the restricted maximum, whether a scaled logit is NaN, and a histogram of the top 12 bits
-    // of every key
-    // (most keys share a few bins: the lanes of a warp with the same bin add once, through their leader)
+    // pass 1: the restricted maximum, whether a scaled logit is NaN, and each thread's two largest values
+    // to order by: the restricted logits themselves where the scaled order is theirs (greedy rows, and
+    // temperatures that are normal positive floats: x -> fl(x / T) does not fall), else the scaled ones
+    const bool raw_order = greedy || p.fast_scale;
     float mx = -kInf;
     int nan_scaled = 0;
-    for (int base = 0; base < width; base += kStep) {  // uniform trip count for the match
-        float v[kShardUnroll];
+    float b0 = -kInf, b1 = -kInf;
+    for (int base = 0; base < width; base += kStep) {
+        float v[kPerStep];
         load_step(base, v);
-#pragma unroll
-        for (int j = 0; j < kShardUnroll; j++) {
-            const int col = base + j * kShardThreads + tid;
-            const bool live = col < width;
-            uint32_t b = 0xFFFFFFFFu;
-            if (live) {
-                const float r = restrict_v(v[j], col);
-                mx = max_nan(mx, r);
-                const float sc = greedy ? r : __fdiv_rn(r, p.temperature);
-                nan_scaled |= !greedy && sc != sc;
-                b = order_key(sc) >> 20;
+#pragma unroll 1
+        for (int j = 0; j < kPerStep; j++) {
+            const int col = col_of(base, j);
+            if (col >= width) continue;
+            const float r = restrict_v(v[j], col);
+            mx = max_nan(mx, r);
+            float o = r;
+            if (!raw_order) {
+                o = __fdiv_rn(r, p.temperature);
+                nan_scaled |= o != o;
+                o = o != o ? kInf : o;  // a NaN row is refused anyway; keep the floor finite-ordered
             }
-            const unsigned peers = __match_any_sync(0xffffffffu, b);
-            if (live && lane == __ffs(peers) - 1) atomicAdd(&s_hist[b], (uint32_t) __popc(peers));
+            if (o > b1) {
+                if (o > b0) b1 = b0, b0 = o;
+                else b1 = o;
+            }
         }
     }
     mx = block_max_nan(mx, s_redf);
+    // with raw order, a scaled logit is NaN only where the restricted one is (a NaN row) or x / T of an
+    // infinite x with a finite T (never NaN): the flag of the other rows is 0
+    if (raw_order && !greedy) nan_scaled = mx != mx;
     nan_scaled = block_or(nan_scaled, s_redi);
     const int take = kk <= sa.k_cap ? kk : 0;  // larger rows are refused by the merge
 
-    // the bin holding the take-th largest key: thread t sums bins [kPer t, kPer t + kPer) from the top
-    constexpr int kPer = kShardBins / kShardThreads;
-    uint32_t mine = 0;
-    for (int j = 0; j < kPer; j++) mine += s_hist[kShardBins - 1 - (tid * kPer + j)];
-    s_scan[tid] = mine;
-    if (tid == 0) s_bin = 0, s_n = 0;
+    // the floor: the take-th largest of the threads' 2 x threads values. take threads hold a value at or
+    // above it, so at least take of the row's elements do: the row's take best are all at or above it
+    // (take <= k_cap <= 1024 <= 2 x threads). Elements whose restricted logit lies below `rb` cannot reach
+    // it (raw_bound) and are not divided at all.
+    s_list[2 * tid] = (uint64_t) order_key(b0) << 32, s_list[2 * tid + 1] = (uint64_t) order_key(b1) << 32;
+    if (tid == 0) s_n = 0;
     __syncthreads();
-    if (tid == 0 && take > 0) {
-        uint32_t above = 0;
-        int t = 0;
-        while (t < kShardThreads && above + s_scan[t] < (uint32_t) take) above += s_scan[t++];
-        int b = kShardBins - 1 - t * kPer;
-        for (int j = 0; j < kPer && b >= 0; j++, b--) {
-            above += s_hist[b];
-            if (above >= (uint32_t) take) break;
-        }
-        s_bin = b < 0 ? 0 : b;
-        s_scan[0] = above;  // keys in bins >= s_bin
+    bitonic_sort_desc(s_list, 2 * kShardThreads);
+    const float fv = take > 0 ? key_value((uint32_t) (s_list[take - 1] >> 32)) : -kInf;  // the take-th largest value
+    uint64_t floor_key;
+    float rb;
+    if (take == 0) {
+        floor_key = ~0ull, rb = kInf;
+    } else if (raw_order) {
+        const float sf = greedy ? fv : __fdiv_rn(fv, p.temperature);
+        floor_key = composite(sf, 0xFFFFFFFFu);  // the least composite of that value
+        rb = greedy ? fv : raw_bound(sf, p.temperature, true);
+    } else {
+        floor_key = composite(fv, 0xFFFFFFFFu), rb = -kInf;
     }
     __syncthreads();
-    const int bin = s_bin;
-    const bool fits = take > 0 && s_scan[0] <= (uint32_t) kShardList;
-    __syncthreads();
-    if (take > 0 && fits) {
-        // pass 2: every key in a bin at or above the bound, then sorted: the first `take` are the best
-        for (int base = 0; base < width; base += kStep) {  // uniform trip count for the ballot
-            float v[kShardUnroll];
-            load_step(base, v);
-#pragma unroll
-            for (int j = 0; j < kShardUnroll; j++) {
-                const int col = base + j * kShardThreads + tid;
-                const uint64_t c = col < width ? key_from(restrict_v(v[j], col), col) : 0ull;
-                const bool in = col < width && (int) (uint32_t) (c >> 52) >= bin;
-                const unsigned m = __ballot_sync(0xffffffffu, in);
-                if (m) {
-                    int at = 0;
-                    if (lane == __ffs(m) - 1) at = atomicAdd(&s_n, __popc(m));
-                    at = __shfl_sync(0xffffffffu, at, __ffs(m) - 1) + __popc(m & ((1u << lane) - 1u));
-                    if (in && at < kShardList) s_list[at] = c;
+    // pass 2: every composite at or above the floor (usually a few times take), then sorted
+    for (int base = 0; base < width && take > 0; base += kStep) {  // uniform trip count for the ballot
+        float v[kPerStep];
+        load_step(base, v);
+#pragma unroll 1
+        for (int j = 0; j < kPerStep; j++) {
+            const int col = col_of(base, j);
+            bool in = false;
+            uint64_t c = 0ull;
+            if (col < width) {
+                const float r = restrict_v(v[j], col);
+                if (r >= rb || r != r || !raw_order) {
+                    c = key_from(r, col);
+                    in = c >= floor_key;
                 }
             }
+            const unsigned m = __ballot_sync(0xffffffffu, in);
+            if (m) {
+                int at = 0;
+                if (lane == __ffs(m) - 1) at = atomicAdd(&s_n, __popc(m));
+                at = __shfl_sync(0xffffffffu, at, __ffs(m) - 1) + __popc(m & ((1u << lane) - 1u));
+                if (in && at < kShardList) s_list[at] = c;
+            }
         }
-        __syncthreads();
-        const int n = s_n < kShardList ? s_n : kShardList;
+    }
+    __syncthreads();
+    const bool fits = s_n <= kShardList;
+    if (take > 0 && fits) {
+        const int n = s_n;
         const int np2 = next_pow2(n);
         for (int i = n + tid; i < np2; i += kShardThreads) s_list[i] = 0ull;
         __syncthreads();
         bitonic_sort_desc(s_list, np2);
     } else if (take > 0) {
-        // too many keys share the bound's bin: radix select over the row, then the selected keys
+        // too many composites at the floor (a row of many equal logits): radix select, then the selected
+        __syncthreads();
+        if (tid == 0) s_n = 0;
         if (take < width) radix_select(width, take, key_of, sel);
         for (int base = 0; base < width; base += kShardThreads) {
             const int col = base + tid;
@@ -290,7 +327,7 @@ __global__ void __launch_bounds__(kShardThreads) shard_merge_kernel(const __grid
 }  // namespace
 
 size_t shard_select_smem_bytes(int bit_words, int hist_slots) {
-    return (size_t) kShardList * 8 + (size_t) kShardBins * 4 + (size_t) bit_words * 4 + (size_t) hist_slots * 8;
+    return (size_t) kShardList * 8 + (size_t) bit_words * 4 + (size_t) hist_slots * 8;
 }
 size_t shard_merge_smem_bytes(int world, int k_cap) {
     return (size_t) next_pow2(world * k_cap) * 8 + (size_t) k_cap * 8;
@@ -298,8 +335,10 @@ size_t shard_merge_smem_bytes(int world, int k_cap) {
 
 cudaError_t launch_shard_select(const ShardArgs & a, bool bf16, cudaStream_t stream) {
     const size_t smem = shard_select_smem_bytes(a.bit_words, a.hist_slots);
-    auto kern = bf16 ? shard_select_kernel<uint16_t> : shard_select_kernel<float>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    const bool vec = reinterpret_cast<uintptr_t>(a.r.logits) % 16 == 0 && (a.r.ld * (bf16 ? 2 : 4)) % 16 == 0;
+    auto kern = bf16 ? (vec ? shard_select_kernel<uint16_t, true> : shard_select_kernel<uint16_t, false>)
+                     : (vec ? shard_select_kernel<float, true> : shard_select_kernel<float, false>);
+    cudaError_t e = ssb::set_max_dynamic_smem((const void *) kern, smem);
     if (e != cudaSuccess) return e;
     kern<<<a.r.rows, kShardThreads, smem, stream>>>(a);
     return cudaGetLastError();
@@ -307,7 +346,7 @@ cudaError_t launch_shard_select(const ShardArgs & a, bool bf16, cudaStream_t str
 
 cudaError_t launch_shard_merge(const ShardArgs & a, cudaStream_t stream) {
     const size_t smem = shard_merge_smem_bytes(a.world, a.k_cap);
-    cudaError_t e = cudaFuncSetAttribute(shard_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    cudaError_t e = ssb::set_max_dynamic_smem((const void *) shard_merge_kernel, smem);
     if (e != cudaSuccess) return e;
     shard_merge_kernel<<<a.r.rows, kShardThreads, smem, stream>>>(a);
     return cudaGetLastError();

@@ -221,7 +221,7 @@ __global__ void __launch_bounds__(kSmallThreads) small_rows_kernel(const SmallAr
 template <typename TIn, bool kDebug>
 cudaError_t launch_small_t(const SmallArgs & a, size_t smem, cudaStream_t stream) {
     auto kern = small_rows_kernel<TIn, kDebug>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    cudaError_t e = ssb::set_max_dynamic_smem((const void *) kern, smem);
     if (e != cudaSuccess) return e;
     kern<<<a.rows, kSmallThreads, smem, stream>>>(a);
     return cudaGetLastError();

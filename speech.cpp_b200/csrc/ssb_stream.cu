@@ -720,7 +720,7 @@ size_t stream_smem_bytes(int mode, bool vec, int chunk, int hist_slots, int cap,
 
 int stream_blocks_per_sm(int mode, bool bf16, bool vec, size_t smem) {
     void * kern = select_kernel(mode, bf16, vec, false);
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem) != cudaSuccess) return 0;
+    if (ssb::set_max_dynamic_smem((const void *) kern, smem) != cudaSuccess) return 0;
     int n = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kStreamThreads, smem) != cudaSuccess) return 0;
     return n;
@@ -729,7 +729,7 @@ int stream_blocks_per_sm(int mode, bool bf16, bool vec, size_t smem) {
 cudaError_t launch_stream(const StreamArgs & a, int mode, bool bf16, bool vec, bool debug, cudaStream_t stream) {
     const size_t smem = stream_smem_bytes(mode, vec, a.chunk, a.hist_slots, a.cap, a.sel_slots);
     void * kern = select_kernel(mode, bf16, vec, debug);
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    cudaError_t e = ssb::set_max_dynamic_smem((const void *) kern, smem);
     if (e != cudaSuccess) return e;
     void * args[] = {const_cast<StreamArgs *>(&a)};
     return cudaLaunchKernel(kern, dim3((unsigned) (a.r.rows * a.splits)), dim3(kStreamThreads), args, smem, stream);

@@ -789,7 +789,7 @@ size_t topk_smem_bytes(int kw, bool bf16, int chunk, int hist_slots, int sel_slo
 
 int topk_blocks_per_sm(int kw, bool bf16, size_t smem) {
     void * kern = pick_kernel(kw, bf16, false);
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem) != cudaSuccess) return 0;
+    if (ssb::set_max_dynamic_smem((const void *) kern, smem) != cudaSuccess) return 0;
     int n = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kTkThreads, smem) != cudaSuccess) return 0;
     return n;
@@ -798,7 +798,7 @@ int topk_blocks_per_sm(int kw, bool bf16, size_t smem) {
 cudaError_t launch_topk(const StreamArgs & a, int kw, bool bf16, bool debug, cudaStream_t stream) {
     const size_t smem = topk_smem_bytes(kw, bf16, a.chunk, a.hist_slots, a.sel_slots);
     void * kern = pick_kernel(kw, bf16, debug);
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    cudaError_t e = ssb::set_max_dynamic_smem((const void *) kern, smem);
     if (e != cudaSuccess) return e;
     void * args[] = {const_cast<StreamArgs *>(&a)};
     return cudaLaunchKernel(kern, dim3((unsigned) (a.r.rows * a.splits)), dim3(kTkThreads), args, smem, stream);
