@@ -36,6 +36,7 @@ constexpr int kBucketBits = 12;
 constexpr int kBuckets = 1 << kBucketBits;
 constexpr int kBucketShift = 32 - kBucketBits;
 constexpr int kListMaxN = 4096;     // tokens of one crossing bucket sorted in shared memory
+constexpr int kQueue = 256;         // pass 1's per-warp queue of a sparse round (kNWarps x kQueue <= 2 kListMaxN)
 constexpr double kMargin = 1e-9;    // relative margin that decides a crossing without the exact path
 constexpr int kChunk = 256;         // exact path: values computed per step by the warp for lane 0's sums
 
@@ -200,6 +201,53 @@ __global__ void __launch_bounds__(kNThreads, 1) nucleus_rows_kernel(const Nucleu
                 if (penal) hbw = s_hbits[w];
             }
             const uint32_t visit = kDebug ? live : allowed;
+            // a sparse round (an allow mask of low density): the warp's visited columns are queued (at most
+            // kQueue, in the still unused list buffer) and taken 32 at a time, one per lane, so that no lane
+            // idles through a chunk that only one lane of the warp has a token in
+            if (!kDebug) {
+                const int nv = __popc(visit);
+                int incl = nv;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += t;
+                }
+                const int total = __shfl_sync(0xffffffffu, incl, 31);
+                if (total <= kQueue) {
+                    int32_t * q = reinterpret_cast<int32_t *>(s_list) + warp_id() * kQueue;
+                    int pos = incl - nv;
+                    for (uint32_t bits = visit; bits; bits &= bits - 1u) q[pos++] = col0 + __ffs(bits) - 1;
+                    __syncwarp();
+                    for (int t0 = 0; t0 < total; t0 += 32) {  // warp-uniform
+                        const int t = t0 + lane;
+                        uint64_t cv = 0;
+                        bool has = false;
+                        if (t < total) {
+                            const int col = q[t];
+                            float v = Elem<TIn>::load1(src, col);
+                            if (penal && ((s_hbits[col >> 5] >> (col & 31)) & 1u)) v = penalized(col, v);
+                            acc = max_nan(acc, v);
+                            const float sc = greedy_row ? v : (pow2 ? __fmul_rn(v, inv_t) : __fdiv_rn(v, T));
+                            nan_scaled |= sc != sc;
+                            if (sc == sc && sc > -kInf) {
+                                cv = composite(sc, (uint32_t) col);
+                                has = true;
+                                best = cv > best ? cv : best;
+                                atomicAdd(&s_hcount[bucket_of(cv)], 1);
+                            }
+                        }
+                        const unsigned m = __ballot_sync(0xffffffffu, has);
+                        if (m) {
+                            int at = 0;
+                            if (lane == __ffs(m) - 1) at = atomicAdd(&s_n, __popc(m));
+                            at = __shfl_sync(0xffffffffu, at, __ffs(m) - 1);
+                            if (has) list[at + __popc(m & ((1u << lane) - 1u))] = cv;
+                        }
+                    }
+                    __syncwarp();
+                    continue;
+                }
+            }
             // the chunks' logits, read together (16-byte loads where the chunk is whole and aligned)
             constexpr int kPerChunk = 8 * (int) sizeof(TIn) / 16;  // 16-byte loads per 8 columns
             uint4 raw[4 * kPerChunk];
