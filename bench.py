@@ -53,9 +53,11 @@ def parse_args():
     ap.add_argument("--density", type=float, default=0.01, help="config 5 allow-mask density")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--path", choices=["sample", "lm-head", "chain"], default="sample",
+    ap.add_argument("--path", choices=["sample", "lm-head", "chain", "shard"], default="sample",
                     help="sample: the sampler on --config (the headline); lm-head: the fused LM head + argmax "
-                         "(--rows, --dim) against cuBLAS + argmax; chain: the device-resident code-predictor chain")
+                         "(--rows, --dim) against cuBLAS + argmax; chain: the device-resident code-predictor chain; "
+                         "shard: the vocabulary-sharded candidate exchange's select and merge on one GPU (--rows, --world)")
+    ap.add_argument("--world", type=int, default=2, help="shard: slices per row")
     ap.add_argument("--dim", type=int, default=2048, help="lm-head: hidden size")
     ap.add_argument("--launches-only", type=int, default=0,
                     help="profiling aid: after the oracle check, issue this many launches and exit (no timing, no JSON)")
@@ -333,10 +335,74 @@ def run_chain(args):
     sampler.close()
 
 
+def run_shard(args):
+    """The candidate exchange's two device steps on one GPU: ssb_shard_select on rank 0's slice of config 4's
+    rows (1 / world of the vocabulary, k_cap 64) and ssb_shard_merge of `world` records, each timed from
+    CUDA-graph replays (device time), beside the whole-row engine on the same rows; the merged ids are
+    checked against the whole-row engine with every slice selected (`--launches-only N`: N selects, no
+    timing, for a profiler)."""
+    import torch
+    import speech_sampler as ss
+    import speech_vocab_shard as vs
+    torch.cuda.set_device(0)
+    rows, world, k_cap = max(1, args.rows or 1), args.world, 64
+    c = wl.config4(rows=rows)
+    p = ss.params(**c["params"])
+    x = torch.from_numpy(c["logits_bf16"]).view(torch.bfloat16).cuda()
+    h = torch.from_numpy(c["history"]).cuda()
+    u = torch.from_numpy(c["u"]).cuda()
+    vocab = x.shape[1]
+    off, width = vs.shard_bounds(vocab, world)[0]
+    sampler = ss.Sampler(0)
+    rec = vs.records_tensor(rows, k_cap, world)
+    if args.launches_only:
+        for _ in range(args.launches_only):
+            sampler.shard_select(x[:, off:off + width], p, off, vocab, k_cap, rec[0], h)
+        torch.cuda.synchronize()
+        return
+    ids_s, st_s = vs.sample_topk_on_one_device(sampler, x, world, p, h, None, ss.MASK_NONE, u, k_cap)
+    ids_w, st_w = sampler.sample(x, p, h, u=u)
+    equal = bool(torch.equal(ids_s, ids_w) and torch.equal(st_s, st_w))
+    stream = torch.cuda.Stream()
+
+    def graph_time(fn, n=20):
+        with torch.cuda.stream(stream):
+            fn()
+            stream.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for _ in range(n):
+                    fn()
+            for _ in range(3):
+                g.replay()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            reps = max(1, args.steps // n)
+            for _ in range(reps):
+                g.replay()
+            b.record(stream)
+        b.synchronize()
+        return a.elapsed_time(b) / (reps * n) * 1e3
+
+    cs = torch.cuda.current_stream
+    t_sel = graph_time(lambda: sampler.shard_select(x[:, off:off + width], p, off, vocab, k_cap, rec[0], h, stream=cs()))
+    t_mer = graph_time(lambda: sampler.shard_merge(rows, p, vocab, world, k_cap, rec, u, stream=cs()))
+    t_whole = graph_time(lambda: sampler.sample(x, p, h, u=u, stream=cs()))
+    print(json.dumps({
+        "metric": "vocabulary-sharded select + merge (device us per call)", "unit": "us",
+        "select_us": t_sel, "merge_us": t_mer, "whole_row_engine_us": t_whole, "higher_is_better": False,
+        "config": {"workload": f"config4 rows: bf16 [{rows}, {vocab}], 1024 history ids, top-k 40; slice 1/{world}",
+                   "k_cap": k_cap, "record_bytes_per_rank": rows * (k_cap + 1) * 8},
+        "ids_equal_whole_row": equal}))
+    sampler.close()
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.path == "shard":
+        return run_shard(args)
     if args.path == "lm-head":
         return run_lm_head(args)
     if args.path == "chain":
