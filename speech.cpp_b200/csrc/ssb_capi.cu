@@ -560,7 +560,20 @@ ssb_status ssb_shard_select(ssb_context * ctx, const ssb_rows * r, int32_t col_o
     a.world = 1;
     a.hist_slots = r->history ? ssb::next_pow2((int) std::max<int64_t>(4, 2 * r->history_ld)) : 0;
     a.records = records;
-    const int words = (int) div_up(r->vocab, 32);
+    // several CTAs per slice row when there are few rows: parts of >= 16384 columns (a part costs a fixed
+    // ~30 us of table, sorts and merge besides its columns), at most two CTAs per SM in all; the parts'
+    // records are merged by the row's last CTA (part records in the split-row scratch, arrivals in the row
+    // counters)
+    int64_t splits = std::min<int64_t>(div_up(r->vocab, 16384), std::max(1, 2 * ctx->sm_count / std::max(1, r->rows)));
+    splits = std::min<int64_t>(splits, ssb::kShardMaxParts / k_cap);
+    while (splits > 1 && (int64_t) r->rows * splits * (k_cap + 1) > (int64_t) ctx->max_slots * ssb::kStreamMaxK) splits--;
+    splits = std::max<int64_t>(1, splits);
+    const int64_t chunk = div_up(div_up(r->vocab, splits), 32) * 32;
+    a.splits = (int) div_up(r->vocab, chunk);
+    a.chunk = (int) chunk;
+    a.parts = ctx->part_cand;
+    a.counters = ctx->counters;
+    const int words = (int) div_up(chunk, 32);
     a.bit_words = r->history && words <= 8192 ? words : 0;  // the bitmap where it fits in 32 KB
     if (ssb::shard_select_smem_bytes(a.bit_words, a.hist_slots) > (size_t) ctx->max_smem) a.bit_words = 0;
     if (ssb::shard_select_smem_bytes(a.bit_words, a.hist_slots) > (size_t) ctx->max_smem)

@@ -122,10 +122,15 @@ struct ShardArgs {
     int k_cap;         // composites per record (a power of two <= 1024)
     int world;         // merge: records per row
     int hist_slots;
-    int bit_words;       // select: words of the history-column bitmap (ceil(width / 32)), or 0
+    int bit_words;       // select: words of the history-column bitmap (ceil(chunk / 32)), or 0
     uint64_t * records;  // select: [rows, k_cap + 1] out; merge: [world][rows][k_cap + 1] in
+    int splits;          // select: CTAs per slice row (splits x k_cap <= 4096), each `chunk` columns
+    int chunk;           //         (a multiple of 32)
+    uint64_t * parts;    //         [rows, splits, k_cap + 1] the parts' records (splits > 1)
+    uint32_t * counters; //         [rows] arrivals, 0 between launches
 };
 constexpr int kShardMaxK = 1024;
+constexpr int kShardMaxParts = 4096;  // splits x k_cap composites merged in shared memory per slice row
 size_t shard_select_smem_bytes(int bit_words, int hist_slots);
 size_t shard_merge_smem_bytes(int world, int k_cap);
 cudaError_t launch_shard_select(const ShardArgs & a, bool bf16, cudaStream_t stream);

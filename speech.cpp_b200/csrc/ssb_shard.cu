@@ -58,17 +58,22 @@ __global__ void __launch_bounds__(kShardThreads) shard_select_kernel(const __gri
     __shared__ SelectState sel;
     __shared__ float s_redf[32];
     __shared__ int s_redi[32];
-    __shared__ int s_n;
+    __shared__ int s_n, s_last;
 
-    const int row = blockIdx.x, tid = (int) threadIdx.x, lane = lane_id();
-    const int width = a.vocab;
+    // this CTA's part of the slice row: columns [c0, c0 + width) of the slice (the whole slice when the
+    // rows are not split)
+    const int split = blockIdx.x, row = blockIdx.y, tid = (int) threadIdx.x, lane = lane_id();
+    const int c0 = split * sa.chunk;
+    const int width = min(a.vocab, c0 + sa.chunk) - c0;
+    const int col_base = sa.col_offset + c0;  // the global index of the part's first column
     const ssb_params pp = a.row_params ? a.row_params[row] : a.params;
     const RowParams p = resolve_params(pp, sa.vocab_total);
     const bool greedy = p.greedy != 0;
     const int want = greedy ? 1 : p.k;
-    const int kk = want < width ? want : width;
+    const int kk = want < width ? want : width;  // this part's best
+    const int kk_row = want < a.vocab ? want : a.vocab;  // the slice row's best
     uint64_t * rec = sa.records + (int64_t) row * (sa.k_cap + 1);
-    const TIn * src = reinterpret_cast<const TIn *>(a.logits) + (int64_t) row * a.ld;
+    const TIn * src = reinterpret_cast<const TIn *>(a.logits) + (int64_t) row * a.ld + c0;
     const int32_t * hist = a.history ? a.history + (int64_t) row * a.history_ld : nullptr;
     int hlen = 0;
     if (hist) {
@@ -76,7 +81,8 @@ __global__ void __launch_bounds__(kShardThreads) shard_select_kernel(const __gri
         hlen = hlen < 0 ? 0 : (hlen > (int) a.history_ld ? (int) a.history_ld : hlen);
     }
     const bool penal = p.history_applies && hlen > 0 && sa.hist_slots > 0;
-    const uint32_t * mrow = (a.mask && a.mask_kind != SSB_MASK_NONE) ? a.mask + (int64_t) row * a.mask_ld : nullptr;
+    const uint32_t * mrow =
+        (a.mask && a.mask_kind != SSB_MASK_NONE) ? a.mask + (int64_t) row * a.mask_ld + (c0 >> 5) : nullptr;
     const int slots = sa.hist_slots;
     const int hbits = slots > 1 ? 31 - __clz(slots) : 1;
     const bool use_bits = penal && sa.bit_words >= ((width + 31) >> 5);
@@ -89,7 +95,7 @@ __global__ void __launch_bounds__(kShardThreads) shard_select_kernel(const __gri
         __syncthreads();
         const uint32_t hmask = (uint32_t) slots - 1u;
         for (int i = tid; i < hlen; i += kShardThreads) {
-            const int32_t g = __ldg(hist + i), t = g - sa.col_offset;
+            const int32_t g = __ldg(hist + i), t = g - col_base;
             if (t < 0 || t >= width || g >= sa.vocab_total) continue;
             uint32_t h = hash_token(t, hbits);
             for (uint32_t n = 0; n <= hmask; n++) {
@@ -114,7 +120,7 @@ __global__ void __launch_bounds__(kShardThreads) shard_select_kernel(const __gri
     };
     auto restricted = [&](int col) { return restrict_v(Elem<TIn>::load1(src, col), col); };
     auto key_from = [&](float r, int col) {
-        return composite(greedy ? r : __fdiv_rn(r, p.temperature), (uint32_t) (sa.col_offset + col));
+        return composite(greedy ? r : __fdiv_rn(r, p.temperature), (uint32_t) (col_base + col));
     };
     auto key_of = [&](int col) { return key_from(restricted(col), col); };
     // kPerStep columns per thread and step, their loads issued together: kShardUnroll scalar loads
@@ -263,8 +269,52 @@ __global__ void __launch_bounds__(kShardThreads) shard_select_kernel(const __gri
         __syncthreads();
         bitonic_sort_desc(s_list, np2);
     }
-    for (int i = tid; i < sa.k_cap; i += kShardThreads) rec[i] = i < take ? s_list[i] : 0ull;
-    if (tid == 0) rec[sa.k_cap] = ((uint64_t) __float_as_uint(mx) << 32) | (uint32_t) nan_scaled;
+    const uint64_t word = ((uint64_t) __float_as_uint(mx) << 32) | (uint32_t) nan_scaled;
+    if (sa.splits == 1) {
+        for (int i = tid; i < sa.k_cap; i += kShardThreads) rec[i] = i < take ? s_list[i] : 0ull;
+        if (tid == 0) rec[sa.k_cap] = word;
+        return;
+    }
+    // split rows: this part's record into the scratch; the row's last CTA to arrive merges the parts'
+    // records (splits x k_cap composites, sorted) into the row's record and leaves the counter at 0
+    uint64_t * part = sa.parts + ((int64_t) row * sa.splits + split) * (sa.k_cap + 1);
+    for (int i = tid; i < sa.k_cap; i += kShardThreads) part[i] = i < take ? s_list[i] : 0ull;
+    __syncthreads();
+    if (tid == 0) {
+        part[sa.k_cap] = word;
+        __threadfence();
+        s_last = atomicAdd(&sa.counters[row], 1u) == (unsigned) (sa.splits - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const int total = sa.splits * sa.k_cap;  // <= kShardList (host)
+    const int tp2 = next_pow2(total);
+    const uint64_t * parts = sa.parts + (int64_t) row * sa.splits * (sa.k_cap + 1);
+    for (int i = tid; i < tp2; i += kShardThreads) {
+        uint64_t c = 0ull;
+        if (i < total) {
+            const int q = i / sa.k_cap, j = i - q * sa.k_cap;
+            c = __ldcg(reinterpret_cast<const unsigned long long *>(parts) + (int64_t) q * (sa.k_cap + 1) + j);
+        }
+        s_list[i] = c;
+    }
+    float gmx = -kInf;
+    int gfl = 0;
+    for (int q = tid; q < sa.splits; q += kShardThreads) {
+        const uint64_t w = __ldcg(reinterpret_cast<const unsigned long long *>(parts) + (int64_t) q * (sa.k_cap + 1) + sa.k_cap);
+        gmx = max_nan(gmx, __uint_as_float((uint32_t) (w >> 32)));
+        gfl |= (int) (uint32_t) w;
+    }
+    gmx = block_max_nan(gmx, s_redf);
+    gfl = block_or(gfl, s_redi);
+    bitonic_sort_desc(s_list, tp2);
+    const int take_row = kk_row <= sa.k_cap ? kk_row : 0;
+    for (int i = tid; i < sa.k_cap; i += kShardThreads) rec[i] = i < take_row ? s_list[i] : 0ull;
+    if (tid == 0) {
+        rec[sa.k_cap] = ((uint64_t) __float_as_uint(gmx) << 32) | (uint32_t) gfl;
+        sa.counters[row] = 0;
+    }
 }
 
 __global__ void __launch_bounds__(kShardThreads) shard_merge_kernel(const __grid_constant__ ShardArgs sa) {
@@ -340,7 +390,7 @@ cudaError_t launch_shard_select(const ShardArgs & a, bool bf16, cudaStream_t str
                      : (vec ? shard_select_kernel<float, true> : shard_select_kernel<float, false>);
     cudaError_t e = ssb::set_max_dynamic_smem((const void *) kern, smem);
     if (e != cudaSuccess) return e;
-    kern<<<a.r.rows, kShardThreads, smem, stream>>>(a);
+    kern<<<dim3(a.splits, a.r.rows), kShardThreads, smem, stream>>>(a);
     return cudaGetLastError();
 }
 
