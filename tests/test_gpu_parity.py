@@ -350,3 +350,42 @@ def test_draw_at_exact_boundaries(engine, oracle):
     want, wst, _ = oracle.sample_rows(c["logits_bf16"], p, history=c["history"], u=u)
     assert_ids(oracle, ids, st, want, wst, c["logits_bf16"], lambda r: p, lambda r: c["history"][r], lambda r: None,
                MASK_NONE, u)
+
+
+def test_context_mask_is_generation_banned(engine):
+    """The talker's suppress mask of Generation::banned (qwen3-tts/sampler.cpp:62-67: the last 1024 ids but
+    the end of speech 2150, and 2150 itself before frame 2) copied once into the context
+    (ssb_context_mask) and used from there by ssb_sample_rows: the same ids as the same mask passed as a
+    tensor, and no banned id drawn."""
+    import ctypes
+    import torch
+    lib = engine.lib
+    V, eos, suppressed, min_frames = wl.TALKER_VOCAB, 2150, 1024, 2
+
+    def banned(frames):
+        b = np.zeros(V, bool)
+        b[V - suppressed:] = True
+        b[eos] = frames < min_frames
+        return b
+
+    t = wl.config2(steps=16)
+    p = ss.params(**t["params"])
+    x = dev(t["logits"])
+    x[:, eos] += 6.0  # the end of speech would win where allowed
+    h, u = dev(t["history"]), dev(t["u"])
+    for frames in (0, 5):
+        words = np.ascontiguousarray(wl.pack_mask(banned(frames)), np.uint32)
+        out = ctypes.c_void_p()
+        assert lib.ssb_context_mask(engine.ctx, ctypes.c_void_p(words.ctypes.data), len(words), ctypes.byref(out)) == ss.OK
+        ids_t, st_t = engine.sample(x, p, h, None, dev(words.view(np.int32)), MASK_BAN, u)
+        ids = torch.empty(16, dtype=torch.int32, device="cuda")
+        st = torch.empty(16, dtype=torch.int32, device="cuda")
+        r = ss.Sampler._rows_struct(x, p, h, None, None, MASK_NONE, u, ids, st)
+        r.mask, r.mask_ld, r.mask_kind = out.value, 0, MASK_BAN
+        assert lib.ssb_sample_rows(engine.ctx, ctypes.byref(r), None) == ss.OK
+        torch.cuda.synchronize()
+        assert torch.equal(ids, ids_t) and torch.equal(st, st_t) and bool(torch.all(st == 0))
+        got = ids.cpu().numpy()
+        assert not banned(frames)[got].any()
+        assert (got == eos).any() == (frames >= min_frames)
+    assert lib.ssb_context_mask(engine.ctx, ctypes.c_void_p(words.ctypes.data), 0, ctypes.byref(out)) == ss.OUT_OF_RANGE
