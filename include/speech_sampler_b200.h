@@ -294,6 +294,12 @@ SSB_API ssb_status ssb_shard_select(ssb_context *ctx, const ssb_rows *slice, int
 SSB_API ssb_status ssb_shard_merge(ssb_context *ctx, const ssb_rows *rows, int32_t vocab_total, int32_t world,
                                    int32_t k_cap, const uint64_t *records, void *stream);
 
+/* The restricted logits (ssb_restrict_rows) of a slice [col_offset, col_offset + slice->vocab) of rows of
+ * vocab_total tokens, taking the rows' GLOBAL history ids and whole-row mask words as ssb_shard_select does:
+ * the first step of the restricted-slice exchange (every row of any top-k, top-k 0 included). */
+SSB_API ssb_status ssb_restrict_slice(ssb_context *ctx, const ssb_rows *slice, int32_t col_offset, int32_t vocab_total,
+                                      float *out, int64_t out_ld, void *stream);
+
 /* ---------------------------------------------------------------- Haru's logit shaping and DRY */
 
 /* DryConfig (haru/sampler.h:37-40, read by file_dry, haru/sampler.cpp:63-73). */

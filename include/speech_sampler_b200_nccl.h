@@ -31,7 +31,12 @@ SSB_API ssb_status ssb_shard_comm_destroy(ssb_shard_comm *comm);
 SSB_API ssb_status ssb_shard_comm_reserve(ssb_shard_comm *comm, int32_t rows, int32_t k_cap);
 
 /* The sharded draw of `slice` (as ssb_shard_select takes it; its ids, status, u and params as
- * ssb_shard_merge takes them) on every rank (collective). */
+ * ssb_shard_merge takes them) on every rank (collective). With k_cap > 0 the candidate exchange (rows of
+ * row_params keeping more than k_cap tokens come back SSB_ROW_INVALID_ROW); with k_cap 0, or without
+ * row_params a drawing row that keeps more than k_cap tokens (top_k 0), the restricted-slice exchange:
+ * ssb_restrict_slice, one ncclAllGather of the f32 slices, the whole rows laid out and ssb_sample_rows on
+ * them (the first such call, and any call with another slice layout, synchronises the stream once to
+ * learn every rank's slice). */
 SSB_API ssb_status ssb_shard_sample(ssb_shard_comm *comm, const ssb_rows *slice, int32_t col_offset,
                                     int32_t vocab_total, int32_t k_cap, void *stream);
 

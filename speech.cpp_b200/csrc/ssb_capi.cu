@@ -694,6 +694,32 @@ ssb_status ssb_restrict_rows(ssb_context * ctx, const ssb_rows * r, float * out,
     return ok();
 }
 
+ssb_status ssb_restrict_slice(ssb_context * ctx, const ssb_rows * r, int32_t col_offset, int32_t vocab_total, float * out,
+                              int64_t out_ld, void * stream) {
+    if (!ctx || !r || !out) return fail(SSB_INVALID_ARGUMENT, "ctx, slice and out are required");
+    if (col_offset < 0 || col_offset % 32 != 0) return fail(SSB_INVALID_ARGUMENT, "col_offset must be a non-negative multiple of 32");
+    if (r->vocab < 1 || (int64_t) col_offset + r->vocab > vocab_total || vocab_total > SSB_MAX_VOCAB)
+        return fail(SSB_INVALID_ARGUMENT, "the slice must lie inside [0, vocab_total)");
+    if (r->rows < 0 || r->ld < r->vocab || out_ld < r->vocab) return fail(SSB_INVALID_ARGUMENT, "rows, ld or out_ld out of order");
+    if (r->dtype != SSB_F32 && r->dtype != SSB_BF16) return fail(SSB_INVALID_ARGUMENT, "dtype is neither SSB_F32 nor SSB_BF16");
+    if (r->mask_kind < SSB_MASK_NONE || r->mask_kind > SSB_MASK_ALLOW) return fail(SSB_INVALID_ARGUMENT, "mask_kind is not an ssb_mask_kind");
+    if (r->mask_kind != SSB_MASK_NONE && (!r->mask || (r->mask_ld > 0 && r->mask_ld < div_up(vocab_total, 32))))
+        return fail(SSB_INVALID_ARGUMENT, "the mask must hold ceil(vocab_total / 32) words per row");
+    if (r->history && (r->history_ld < 0 || r->history_ld > SSB_MAX_STREAM_HISTORY))
+        return fail(SSB_OUT_OF_RANGE, "history_ld must lie in [0, SSB_MAX_STREAM_HISTORY]");
+    if (r->rows == 0) return ok();
+    if (!r->logits) return fail(SSB_INVALID_ARGUMENT, "logits is null");
+    ssb_status s = use_device(ctx);
+    if (s != SSB_OK) return s;
+    ssb::RowsArgs a = rows_args(r, 1, nullptr);
+    a.mask = r->mask_kind != SSB_MASK_NONE ? r->mask + col_offset / 32 : nullptr;
+    const int hist_slots = r->history && r->history_ld > 0 ? ssb::next_pow2((int) std::max<int64_t>(4, 2 * r->history_ld)) : 0;
+    const cudaError_t e = ssb::launch_restrict(a, hist_slots, r->dtype == SSB_BF16, out, out_ld, ctx->sm_count,
+                                               static_cast<cudaStream_t>(stream), col_offset, vocab_total);
+    if (e != cudaSuccess) return cuda_fail(e, "restrict launch");
+    return ok();
+}
+
 ssb_status ssb_sample_host(ssb_context * ctx, const ssb_rows * rows, void * stream_ptr) {
     Plan plan{};
     ssb_status s = check_rows(rows, false, &plan);

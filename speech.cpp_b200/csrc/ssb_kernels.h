@@ -207,7 +207,9 @@ cudaError_t launch_haru_shape(const ShapeArgs & a, cudaStream_t stream);
 // The restricted logits alone (ssb_restrict.cu): every column widened to f32 with the mask applied,
 // then each row's history tokens penalized over it. `a` needs no ids, status or u.
 size_t restrict_smem_bytes(int hist_slots);
+// col_offset / vocab_total: the rows are columns [col_offset, col_offset + a.vocab) of rows of vocab_total
+// tokens whose history holds the whole rows' ids (0 / 0: the whole rows).
 cudaError_t launch_restrict(const RowsArgs & a, int hist_slots, bool bf16, float * out, int64_t out_ld, int sm_count,
-                            cudaStream_t stream);
+                            cudaStream_t stream, int col_offset = 0, int vocab_total = 0);
 
 }  // namespace ssb

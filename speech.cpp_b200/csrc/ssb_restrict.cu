@@ -36,7 +36,7 @@ __global__ void __launch_bounds__(kRestrictThreads) restrict_copy_kernel(const R
 
 template <typename TIn>
 __global__ void __launch_bounds__(kRestrictThreads) restrict_history_kernel(const RowsArgs a, int hist_slots, float * out,
-                                                                            int64_t out_ld) {
+                                                                            int64_t out_ld, int col_offset, int vocab_total) {
     extern __shared__ int32_t s_table[];
     int32_t * s_key = s_table;               // [hist_slots] ids, -1 empty
     int32_t * s_cnt = s_table + hist_slots;  // [hist_slots] occurrences
@@ -54,8 +54,9 @@ __global__ void __launch_bounds__(kRestrictThreads) restrict_history_kernel(cons
         for (int i = threadIdx.x; i < hist_slots; i += blockDim.x) s_key[i] = -1, s_cnt[i] = 0;
         __syncthreads();
         for (int i = threadIdx.x; i < hlen; i += blockDim.x) {
-            const int32_t t = __ldg(hist + i);
-            if (t < 0 || t >= a.vocab) continue;  // ids outside the vocabulary are not tokens of the row
+            // history ids are the whole row's; the rows here may be a slice starting at col_offset
+            const int32_t g = __ldg(hist + i), t = g - col_offset;
+            if (g < 0 || g >= vocab_total || t < 0 || t >= a.vocab) continue;
             uint32_t h = hash_token(t, bits);
             for (uint32_t n = 0; n <= hmask; n++) {
                 const int32_t old = atomicCAS(&s_key[h], -1, t);
@@ -82,7 +83,8 @@ __global__ void __launch_bounds__(kRestrictThreads) restrict_history_kernel(cons
 size_t restrict_smem_bytes(int hist_slots) { return (size_t) hist_slots * 8; }
 
 cudaError_t launch_restrict(const RowsArgs & a, int hist_slots, bool bf16, float * out, int64_t out_ld, int sm_count,
-                            cudaStream_t stream) {
+                            cudaStream_t stream, int col_offset, int vocab_total) {
+    if (vocab_total <= 0) vocab_total = a.vocab;
     const int col_blocks = (int) std::min<int64_t>((a.vocab + kRestrictThreads - 1) / kRestrictThreads, 4 * sm_count);
     const dim3 grid((unsigned) std::max(1, col_blocks), (unsigned) std::min(a.rows, 65535));
     if (bf16) restrict_copy_kernel<uint16_t><<<grid, kRestrictThreads, 0, stream>>>(a, out, out_ld);
@@ -95,8 +97,8 @@ cudaError_t launch_restrict(const RowsArgs & a, int hist_slots, bool bf16, float
     e = ssb::set_max_dynamic_smem((const void *) kern, smem);
     if (e != cudaSuccess) return e;
     const int blocks = std::min(a.rows, 4 * sm_count);
-    if (bf16) restrict_history_kernel<uint16_t><<<blocks, kRestrictThreads, smem, stream>>>(a, hist_slots, out, out_ld);
-    else restrict_history_kernel<float><<<blocks, kRestrictThreads, smem, stream>>>(a, hist_slots, out, out_ld);
+    if (bf16) restrict_history_kernel<uint16_t><<<blocks, kRestrictThreads, smem, stream>>>(a, hist_slots, out, out_ld, col_offset, vocab_total);
+    else restrict_history_kernel<float><<<blocks, kRestrictThreads, smem, stream>>>(a, hist_slots, out, out_ld, col_offset, vocab_total);
     return cudaGetLastError();
 }
 

@@ -146,6 +146,8 @@ def load_library(path: str = LIB_PATH):
     lib.ssb_sample_host.argtypes = [vp, ctypes.POINTER(Rows), vp]
     lib.ssb_restrict_rows.restype = ctypes.c_int
     lib.ssb_restrict_rows.argtypes = [vp, ctypes.POINTER(Rows), vp, ctypes.c_int64, vp]
+    lib.ssb_restrict_slice.restype = ctypes.c_int
+    lib.ssb_restrict_slice.argtypes = [vp, ctypes.POINTER(Rows), i32, i32, vp, ctypes.c_int64, vp]
     lib.ssb_shard_record_words.restype = ctypes.c_int64
     lib.ssb_shard_record_words.argtypes = [i32, i32]
     lib.ssb_shard_select.restype = ctypes.c_int
@@ -294,6 +296,16 @@ class Sampler:
         s = None if stream is None else ctypes.c_void_p(stream.cuda_stream)
         _check(self.lib, self.lib.ssb_shard_select(self.ctx, ctypes.byref(r), col_offset, vocab_total, k_cap,
                                                   _dptr(records), s))
+
+    def restrict_slice(self, logits_slice, p, col_offset: int, vocab_total: int, out, history=None, mask=None,
+                       mask_kind=MASK_NONE, row_params=None, stream=None):
+        """ssb_restrict_slice: the restricted logits of this slice into `out` (f32 [rows, >= width]); history
+        holds the rows' global ids, mask the whole rows' words."""
+        r = self._rows_struct(logits_slice, p, history, None, mask, mask_kind, None, None, None, row_params)
+        s = None if stream is None else ctypes.c_void_p(stream.cuda_stream)
+        _check(self.lib, self.lib.ssb_restrict_slice(self.ctx, ctypes.byref(r), col_offset, vocab_total, _dptr(out),
+                                                    out.stride(0), s))
+        return out
 
     def shard_merge(self, rows: int, p, vocab_total: int, world: int, k_cap: int, records, u=None, row_params=None,
                     ids=None, status=None, stream=None):

@@ -310,6 +310,31 @@ def _main_topk():
             t = torch.tensor([float(np.median(times)), 0.0 if equal else 1.0], device="cuda")
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             out[rows] = (float(t[0]), bool(t[1] == 0))
+        # top-k 0 rows (config 5: allow masks, top-p 0.9) through the same call: the restricted-slice
+        # exchange inside the C++ library
+        c5 = wl.config5(rows=8, density=0.01)
+        p5 = ss.params(**c5["params"])
+        x5 = torch.from_numpy(c5["logits"]).cuda()
+        m5 = torch.from_numpy(c5["mask"].view(np.int32)).cuda()
+        u5 = torch.from_numpy(c5["u"]).cuda()
+        off5, width5 = shard_bounds(x5.shape[1], world)[rank]
+        ids_w5, st_w5 = sampler.sample(x5, p5, None, None, m5, ss.MASK_ALLOW, u5)
+        times5 = []
+        for rep in range(15):
+            dist.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            e0.record(stream)
+            ids_s5, st_s5 = comm.sample(x5[:, off5:off5 + width5], p5, off5, x5.shape[1], k_cap, mask=m5,
+                                        mask_kind=ss.MASK_ALLOW, u=u5, stream=stream)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            if rep >= 5:
+                times5.append(e0.elapsed_time(e1) * 1e3)
+        eq5 = bool(torch.equal(ids_w5, ids_s5) and torch.equal(st_w5, st_s5))
+        t5 = torch.tensor([float(np.median(times5)), 0.0 if eq5 else 1.0], device="cuda")
+        dist.all_reduce(t5, op=dist.ReduceOp.MAX)
+        out["config5 top-k 0, 8 rows (restricted-slice exchange)"] = (float(t5[0]), bool(t5[1] == 0))
         if rank == 0:
             print(json.dumps({"vocab_sharded": "candidate exchange (NCCL)", "ranks": world, "vocab": vocab,
                               "k_cap": k_cap, "workload": "config 4 rows (bf16, 1024 history ids, top-k 40)",

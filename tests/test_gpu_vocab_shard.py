@@ -139,3 +139,24 @@ def test_exchange_statuses_and_row_params(engine):
                                              ss.ROW_TEMPERATURE_OVERFLOW, ss.ROW_OK]
     assert i_s[4] == iw[4]
     assert s_s[5] == ss.ROW_INVALID_ROW and i_s[5] == -1
+
+
+def test_restrict_slice_with_global_history(engine):
+    """ssb_restrict_slice (the restricted-slice exchange's first step, history as the rows' global ids, the
+    whole rows' mask) equals the whole rows' restricted logits on the slice's columns, bit for bit."""
+    import torch
+    c = wl.config4(rows=4)
+    x = dev(c["logits_bf16"], torch.bfloat16)
+    h = dev(c["history"])
+    V = x.shape[1]
+    ban = np.zeros((4, V), bool)
+    ban[:, ::97] = True
+    m = dev(wl.pack_mask(ban).view(np.int32))
+    p = ss.params(**c["params"])
+    whole = engine.restrict(x, p, h, None, m, ss.MASK_BAN)
+    for world in (2, 3, 8):
+        for off, width in vs.shard_bounds(V, world):
+            out = torch.empty((4, width), dtype=torch.float32, device="cuda")
+            engine.restrict_slice(x[:, off:off + width], p, off, V, out, h, m, ss.MASK_BAN)
+            torch.cuda.synchronize()
+            assert torch.equal(out.view(torch.int32), whole[:, off:off + width].contiguous().view(torch.int32)), (world, off)
