@@ -10,7 +10,7 @@
 //   pass 1  the row: restricted (penalties, mask) and scaled logits; every token with a finite scaled
 //           logit goes to a per-CTA list in global memory as its composite key (value, then lowest index).
 //   pass 2  the list: w = exp(s - max) in double, its total, and a histogram of that mass (and of the
-//           token counts) over the top 12 bits of the scaled logit's order key.
+//           token counts) over buckets linear in max - s (1/64 wide; mass_bucket).
 //   cut     scanning the histogram from the top finds the bucket where the running share reaches top_p;
 //           its tokens are sorted in shared memory and scanned, which gives keep and pick()'s total;
 //   draw    the same for the running sum u * total: its bucket, sorted and scanned, gives chosen.
@@ -41,6 +41,15 @@ constexpr double kMargin = 1e-9;    // relative margin that decides a crossing w
 constexpr int kChunk = 256;         // exact path: values computed per step by the warp for lane 0's sums
 
 __device__ __forceinline__ uint32_t bucket_of(uint64_t c) { return (uint32_t) (c >> 32) >> kBucketShift; }
+
+// Bucket of a candidate's mass: linear in the distance of its scaled logit below the row's maximum mxf,
+// 1/64 per bucket from the top bucket down (every candidate 64 or more below shares bucket 0). Like
+// bucket_of it never decreases along the composite order, and it is far finer where the mass lies: the
+// top 12 key bits hold only 3 mantissa bits, so logits of a few units spread over a few dozen buckets.
+__device__ __forceinline__ uint32_t mass_bucket(uint64_t c, float mxf) {
+    const float d = __fmul_rn(__fsub_rn(mxf, composite_value(c)), 64.0f);
+    return d >= (float) (kBuckets - 1) ? 0u : (uint32_t) (kBuckets - 1) - (uint32_t) d;
+}
 
 // Block-wide inclusive scan of one double per thread (blockDim = kNThreads); `s` holds kNWarps doubles.
 __device__ __forceinline__ double block_scan_incl(double v, double * s) {
@@ -337,6 +346,7 @@ __global__ void __launch_bounds__(kNThreads, 1) nucleus_rows_kernel(const Nucleu
             continue;
         }
         const double mx = (double) composite_value(best);
+        const float mxf = composite_value(best);
         const double u = a.u ? a.u[row] : 0.0;
         const double tp = p.top_p < 1.0f ? (double) p.top_p : 2.0;  // 2: no cut
         const int kk = p.k;  // the candidates: the kk best (kk may exceed n: the rest are -inf)
@@ -385,13 +395,13 @@ __global__ void __launch_bounds__(kNThreads, 1) nucleus_rows_kernel(const Nucleu
         };
         // Sorts bucket b's tokens of the list (descending) into s_list; returns their count, or -1 if too
         // many for shared memory.
-        auto load_bucket = [&](int b, uint64_t floor) {
+        auto load_bucket = [&](int b, uint64_t floor, bool by_mass) {
             if (tid == 0) s_lc = 0;
             __syncthreads();
             for (int base = 0; base < n; base += kNThreads) {  // uniform trip count: the ballot needs every lane
                 const int i = base + tid;
                 const uint64_t c = i < n ? __ldcg(reinterpret_cast<const unsigned long long *>(list + i)) : 0ull;
-                const bool in = i < n && (int) bucket_of(c) == b && c >= floor;
+                const bool in = i < n && (int) (by_mass ? mass_bucket(c, mxf) : bucket_of(c)) == b && c >= floor;
                 const unsigned m = __ballot_sync(0xffffffffu, in);
                 if (m) {
                     int at = 0;
@@ -437,7 +447,7 @@ __global__ void __launch_bounds__(kNThreads, 1) nucleus_rows_kernel(const Nucleu
             return -1;
         };
 
-        bool exact = kDebug;
+        bool exact = kDebug || !(mxf > -kInf && mxf < kInf);  // the mass buckets need a finite maximum
         // the kk-th best composite: the candidates are those at or above it (every finite one when kk >= n)
         uint64_t kth = 0;
         if (!exact && kk < n) {
@@ -452,7 +462,7 @@ __global__ void __launch_bounds__(kNThreads, 1) nucleus_rows_kernel(const Nucleu
             __syncthreads();
             const int bk = s_i0;
             const int above = bk >= 0 ? s_hcount[bk] : 0;
-            const int cnt = bk >= 0 ? load_bucket(bk, 0ull) : -1;
+            const int cnt = bk >= 0 ? load_bucket(bk, 0ull, false) : -1;
             if (cnt < 0 || kk - above - 1 >= cnt) exact = true;
             else kth = s_list[kk - above - 1];
             __syncthreads();
@@ -468,7 +478,7 @@ __global__ void __launch_bounds__(kNThreads, 1) nucleus_rows_kernel(const Nucleu
                 if (c < kth) continue;
                 const double e = exp((double) composite_value(c) - mx);
                 part += e;
-                const uint32_t b = bucket_of(c);
+                const uint32_t b = mass_bucket(c, mxf);
                 atomicAdd(&s_hmass[b], e);
                 atomicAdd(&s_hcount[b], 1);
             }
@@ -487,7 +497,7 @@ __global__ void __launch_bounds__(kNThreads, 1) nucleus_rows_kernel(const Nucleu
             if (b1 == -1) {
                 exact = true;
             } else if (b1 >= 0) {
-                const int cnt = load_bucket(b1, kth);
+                const int cnt = load_bucket(b1, kth, true);
                 if (cnt < 0) {
                     exact = true;
                 } else {
@@ -514,7 +524,7 @@ __global__ void __launch_bounds__(kNThreads, 1) nucleus_rows_kernel(const Nucleu
                 if (b2 < 0) {
                     exact = true;
                 } else {
-                    const int cnt = load_bucket(b2, kth);
+                    const int cnt = load_bucket(b2, kth, true);
                     if (cnt < 0) {
                         exact = true;
                     } else {

@@ -39,6 +39,27 @@ def test_every_token_no_mask(engine, oracle):
         assert_ids(oracle, ids, st, want, wst, x, lambda r: p, lambda r: None, lambda r: None, MASK_NONE, u)
 
 
+@pytest.mark.parametrize("scale,kw", [
+    (30.0, dict(temperature=1.0, top_k=0, top_p=0.9)),      # most tokens 64 or more below the maximum
+    (30.0, dict(temperature=1.0, top_k=0, top_p=0.999)),
+    (2.0, dict(temperature=0.05, top_k=0, top_p=0.9)),      # a small temperature: the same spread, scaled
+    (0.01, dict(temperature=1.0, top_k=0, top_p=0.9)),      # nearly flat: the mass in a handful of buckets
+])
+def test_mass_spread(engine, oracle, scale, kw):
+    """The mass histogram's buckets are 1/64 wide below the row's maximum scaled logit, and every token
+    64 or more below shares the lowest: rows far wider and far narrower than that."""
+    rng = np.random.default_rng(int(scale * 100) + int(kw["top_p"] * 1000))
+    x = (rng.standard_normal((4, 151936), dtype=np.float32) * np.float32(scale))
+    allow = rng.random((4, 151936)) < 0.5
+    mask = wl.pack_mask(allow)
+    u = rng.random(4)
+    p = params(**kw)
+    ids, st = engine_run(engine, x, ss.params(**kw), mask=mask, mask_kind=MASK_ALLOW, u=u)
+    want, wst, _ = oracle.sample_rows(x, p, mask=mask, mask_kind=MASK_ALLOW, u=u)
+    near = assert_ids(oracle, ids, st, want, wst, x, lambda r: p, lambda r: None, lambda r: mask[r], MASK_ALLOW, u)
+    assert near == 0
+
+
 def test_bf16_history_large_k(engine, oracle):
     c = wl.config4(rows=4)
     kw = dict(c["params"], top_k=2000)

@@ -252,6 +252,41 @@ def test_stream_variants(engine, oracle, rows, vocab, kw):
         assert np.array_equal(ids, want_ids), (ld, ids, want_ids)
 
 
+def _one_warp_allow(rows, vocab, g):
+    """Allow mask keeping only the columns whose 16-byte group i has i % 256 < 32: in a one-CTA row of the
+    top-k kernel those are the groups of the first consumer warp (group i goes to consumer lane i % 256),
+    so every other warp sees only masked tokens."""
+    cols = np.arange(vocab)
+    return np.broadcast_to(((cols // g) % 256) < 32, (rows, vocab))
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+@pytest.mark.parametrize("shape", ["one-warp-allow", "ascending", "negative-temperature"])
+def test_topk_rare_paths(engine, oracle, bf16, shape):
+    """Rows that no random batch produces, 160 of them (one CTA per row): allowed tokens that only one
+    consumer warp streams, a row whose logits rise from its first column to its last (every block a new
+    maximum), and a negative temperature (the order reversed, so no raw bound applies)."""
+    rows, vocab = 160, 151936
+    rng = np.random.default_rng(7 + bf16 + 10 * len(shape))
+    x = (rng.standard_normal((rows, vocab)) * 3).astype(np.float32)
+    mask, kind = None, MASK_NONE
+    kw = dict(temperature=0.8, top_k=40, top_p=0.95, presence_penalty=0.5, frequency_penalty=0.3)
+    if shape == "one-warp-allow":
+        mask, kind = wl.pack_mask(_one_warp_allow(rows, vocab, 8 if bf16 else 4)), MASK_ALLOW
+    elif shape == "ascending":
+        x = (np.linspace(-20, 20, vocab, dtype=np.float32)[None, :] + 1e-3 * x).astype(np.float32)
+    else:
+        kw = dict(temperature=-0.7, top_k=40, top_p=0.9, repetition_penalty=1.1)
+    logits = wl.to_bf16_bits(x) if bf16 else x
+    hist = rng.integers(0, vocab, size=(rows, 256)).astype(np.int32)
+    u = rng.random(rows)
+    want, wst, _ = oracle.sample_rows(logits, params(**kw), history=hist, mask=mask, mask_kind=kind, u=u)
+    ids, st = engine_run(engine, logits, ss.params(**kw), hist, mask=mask, mask_kind=kind, u=u)
+    near = assert_ids(oracle, ids, st, want, wst, logits, lambda r: params(**kw), lambda r: hist[r],
+                      lambda r: None if mask is None else mask[r], kind, u)
+    assert near == 0
+
+
 def test_row_params_mixed(engine, oracle):
     rng = np.random.default_rng(7)
     rows, vocab = 6, 151936
