@@ -6,7 +6,8 @@
 //   2. repetition penalty once per distinct in-range history id (:33-39; a shared count table plays the
 //      reference's `seen` bitmap), then the presence/frequency extension;
 //   3. ban/allow mask -> -inf (:40-42);
-//   4. max -> PENALTY_OVERFLOW / NO_FINITE_LOGIT (:43-49), NaN -> NON_FINITE_INPUT;
+//   4. max -> PENALTY_OVERFLOW / NO_FINITE_LOGIT (:43-49), NaN -> NON_FINITE_INPUT (steps 2-5's per-element
+//      work is one pass; the row's statistics meet in one shared atomic per warp);
 //   5. greedy: first maximum (:105-108); else scale by the temperature (:73), top-k (k <= 128: the k-th
 //      largest 16-bit key from two histograms, the composites reaching it ranked; otherwise a radix select
 //      on composite keys and a sort of the k), softmax in double, top-p, pick (:76-99, sampling.cpp:9-19).
@@ -25,9 +26,6 @@ template <typename TIn, bool kDebug>
 __global__ void __launch_bounds__(kSmallThreads) small_rows_kernel(const SmallArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ SelectState sel;
-    __shared__ float s_redf[32];
-    __shared__ uint64_t s_red64[32];
-    __shared__ int s_redi[32];
 
     const int row = blockIdx.x;
     const int vocab = a.vocab;
@@ -76,6 +74,16 @@ __global__ void __launch_bounds__(kSmallThreads) small_rows_kernel(const SmallAr
         }
     }
 
+    const bool fastk = !p.greedy && p.k <= kFastK;
+    __shared__ __align__(16) uint32_t s_h1[256];
+    __shared__ __align__(16) uint32_t s_h2[256];
+    __shared__ uint32_t s_rawkey;           // the largest order key of a non-NaN restricted logit (0: none)
+    __shared__ int s_flags;                 // bit 0: a NaN restricted logit; bit 1: a NaN scaled logit
+    __shared__ unsigned long long s_best;   // greedy: the largest composite of the restricted logits
+    __shared__ int s_nc;
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) s_h1[i] = 0, s_h2[i] = 0;
+    if (threadIdx.x == 0) s_rawkey = 0, s_flags = 0, s_best = 0ull, s_nc = 0;
+
     // ---- penalties over the history
     if (penal) {
         for (int i = threadIdx.x; i < vocab; i += blockDim.x) s_cnt[i] = 0;
@@ -87,9 +95,12 @@ __global__ void __launch_bounds__(kSmallThreads) small_rows_kernel(const SmallAr
     }
     __syncthreads();
 
-    // ---- penalties, mask, processed output, row statistics
+    // ---- one pass: penalties, mask, processed output and the row's statistics; for a drawing row the
+    // logits scaled by the temperature (qwen3-tts/sampler.cpp:73, every logit, -inf included, divided in
+    // fp32) and counted in the first key histogram. The statistics meet in one shared atomic per warp.
     const uint32_t * mrow = (a.mask && a.mask_kind != SSB_MASK_NONE) ? a.mask + (int64_t) row * a.mask_ld : nullptr;
-    float raw_max = -kInf;
+    uint32_t mkey = 0;
+    int flags = 0;
     uint64_t best = 0;  // greedy: composite of the unscaled value (first maximum = lowest index on ties)
     for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
         float v = s_val[i];
@@ -98,13 +109,30 @@ __global__ void __launch_bounds__(kSmallThreads) small_rows_kernel(const SmallAr
             if (c) v = penalize(v, (int) c, p);
         }
         if (mrow && masked_bit(mrow[i >> 5] >> (i & 31), a.mask_kind)) v = -kInf;
-        s_val[i] = v;
         if (kDebug && a.dbg_processed) a.dbg_processed[(int64_t) row * vocab + i] = v;
-        raw_max = max_nan(raw_max, v);
-        const uint64_t c = composite(v, (uint32_t) i);
-        best = c > best ? c : best;
+        if (v != v) flags |= 1;
+        else mkey = max(mkey, order_key(v));
+        if (p.greedy) {
+            const uint64_t c = composite(v, (uint32_t) i);
+            best = c > best ? c : best;
+        } else {
+            const float sc = __fdiv_rn(v, p.temperature);
+            if (sc != sc) flags |= 2;
+            s_val[i] = sc;
+            if (fastk) red_bin(s_h1, true, order_key(sc) >> 24);
+        }
     }
-    raw_max = block_max_nan(raw_max, s_redf);
+    mkey = __reduce_max_sync(0xffffffffu, mkey);
+    flags = (int) __reduce_or_sync(0xffffffffu, (unsigned) flags);
+    if (p.greedy) best = warp_max_u64(best);
+    if (lane_id() == 0) {
+        atomicMax(&s_rawkey, mkey);
+        if (flags) atomicOr(&s_flags, flags);
+        if (p.greedy) atomicMax(&s_best, (unsigned long long) best);
+    }
+    __syncthreads();
+    const int row_flags = s_flags;
+    const float raw_max = (row_flags & 1) ? __uint_as_float(0x7FC00000u) : key_value(s_rawkey);
     const int st = restricted_status(raw_max, p.rep);
     if (st != SSB_ROW_OK) {
         if (threadIdx.x == 0) {
@@ -114,24 +142,14 @@ __global__ void __launch_bounds__(kSmallThreads) small_rows_kernel(const SmallAr
         return;
     }
     if (p.greedy) {
-        best = block_max_u64(best, s_red64);
         if (threadIdx.x == 0) {
-            *id_out = (int32_t) composite_index(best), *status_out = SSB_ROW_OK;
+            *id_out = (int32_t) composite_index(s_best), *status_out = SSB_ROW_OK;
             if (out.count) *out.count = 1;
             if (out.tokens && out.cap > 0) out.tokens[0] = *id_out, out.weights[0] = 1.0;
         }
         return;
     }
-
-    // ---- temperature (qwen3-tts/sampler.cpp:73): every logit, including -inf, divided in fp32
-    int nan_scaled = 0;
-    for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
-        const float s = __fdiv_rn(s_val[i], p.temperature);
-        nan_scaled |= s != s;
-        s_val[i] = s;
-    }
-    nan_scaled = block_or(nan_scaled, s_redi);
-    if (nan_scaled) {
+    if (row_flags & 2) {
         if (threadIdx.x == 0) {
             *id_out = -1, *status_out = SSB_ROW_TEMPERATURE_OVERFLOW;
             if (out.count) *out.count = 0;
@@ -141,17 +159,10 @@ __global__ void __launch_bounds__(kSmallThreads) small_rows_kernel(const SmallAr
 
     const int k = p.k;
     const double u = a.u ? a.u[row] : 0.0;
-    if (k <= kFastK) {
-        // ---- top-k by the k-th largest 16-bit key (two 256-bin histograms: high byte, then low byte), the
-        // composites whose key reaches it (the k best and their ties at 16 bits), ranked (s_cnt's space)
-        __shared__ __align__(16) uint32_t s_h1[256];
-        __shared__ __align__(16) uint32_t s_h2[256];
-        __shared__ int s_nc;
-        for (int i = threadIdx.x; i < 256; i += blockDim.x) s_h1[i] = 0, s_h2[i] = 0;
-        if (threadIdx.x == 0) s_nc = 0;
-        __syncthreads();
-        for (int i = threadIdx.x; i < vocab; i += blockDim.x) red_bin(s_h1, true, order_key(s_val[i]) >> 24);
-        __syncthreads();
+    if (fastk) {
+        // ---- top-k by the k-th largest 16-bit key (two 256-bin histograms: high byte, counted above,
+        // then low byte), the composites whose key reaches it (the k best and their ties at 16 bits),
+        // ranked (s_cnt's space)
         uint32_t above1 = 0;
         const int b1 = top_bin(s_h1, (uint32_t) k, &above1);  // the histogram holds vocab >= k keys
         for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
