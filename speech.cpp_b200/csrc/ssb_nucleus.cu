@@ -39,6 +39,7 @@ constexpr int kListMaxN = 4096;     // tokens of one crossing bucket sorted in s
 constexpr int kQueue = 256;         // pass 1's per-warp queue of a sparse round (kNWarps x kQueue <= 2 kListMaxN)
 constexpr double kMargin = 1e-9;    // relative margin that decides a crossing without the exact path
 constexpr int kChunk = 256;         // exact path: values computed per step by the warp for lane 0's sums
+constexpr int kScanUnroll = 8;      // list entries requested together per thread by the list scans
 
 __device__ __forceinline__ uint32_t bucket_of(uint64_t c) { return (uint32_t) (c >> 32) >> kBucketShift; }
 
@@ -398,17 +399,27 @@ __global__ void __launch_bounds__(kNThreads, 1) nucleus_rows_kernel(const Nucleu
         auto load_bucket = [&](int b, uint64_t floor, bool by_mass) {
             if (tid == 0) s_lc = 0;
             __syncthreads();
-            for (int base = 0; base < n; base += kNThreads) {  // uniform trip count: the ballot needs every lane
-                const int i = base + tid;
-                const uint64_t c = i < n ? __ldcg(reinterpret_cast<const unsigned long long *>(list + i)) : 0ull;
-                const bool in = i < n && (int) (by_mass ? mass_bucket(c, mxf) : bucket_of(c)) == b && c >= floor;
-                const unsigned m = __ballot_sync(0xffffffffu, in);
-                if (m) {
-                    int at = 0;
-                    if (lane == __ffs(m) - 1) at = atomicAdd(&s_lc, __popc(m));
-                    at = __shfl_sync(0xffffffffu, at, __ffs(m) - 1);
-                    const int pos = at + __popc(m & ((1u << lane) - 1u));
-                    if (in && pos < kListMaxN) s_list[pos] = c;
+            // uniform trip count (the ballot needs every lane); kScanUnroll entries in flight per thread
+            for (int base = 0; base < n; base += kNThreads * kScanUnroll) {
+                uint64_t cs[kScanUnroll];
+#pragma unroll
+                for (int q = 0; q < kScanUnroll; q++) {
+                    const int i = base + q * kNThreads + tid;
+                    cs[q] = i < n ? __ldcg(reinterpret_cast<const unsigned long long *>(list + i)) : 0ull;
+                }
+#pragma unroll
+                for (int q = 0; q < kScanUnroll; q++) {
+                    const int i = base + q * kNThreads + tid;
+                    const uint64_t c = cs[q];
+                    const bool in = i < n && (int) (by_mass ? mass_bucket(c, mxf) : bucket_of(c)) == b && c >= floor;
+                    const unsigned m = __ballot_sync(0xffffffffu, in);
+                    if (m) {
+                        int at = 0;
+                        if (lane == __ffs(m) - 1) at = atomicAdd(&s_lc, __popc(m));
+                        at = __shfl_sync(0xffffffffu, at, __ffs(m) - 1);
+                        const int pos = at + __popc(m & ((1u << lane) - 1u));
+                        if (in && pos < kListMaxN) s_list[pos] = c;
+                    }
                 }
             }
             __syncthreads();
@@ -473,14 +484,23 @@ __global__ void __launch_bounds__(kNThreads, 1) nucleus_rows_kernel(const Nucleu
             for (int i = tid; i < kBuckets; i += kNThreads) s_hmass[i] = 0.0, s_hcount[i] = 0;
             __syncthreads();
             double part = 0.0;
-            for (int i = tid; i < n; i += kNThreads) {
-                const uint64_t c = __ldcg(reinterpret_cast<const unsigned long long *>(list + i));
-                if (c < kth) continue;
-                const double e = exp((double) composite_value(c) - mx);
-                part += e;
-                const uint32_t b = mass_bucket(c, mxf);
-                atomicAdd(&s_hmass[b], e);
-                atomicAdd(&s_hcount[b], 1);
+            for (int base = 0; base < n; base += kNThreads * kScanUnroll) {  // kScanUnroll entries in flight
+                uint64_t cs[kScanUnroll];
+#pragma unroll
+                for (int q = 0; q < kScanUnroll; q++) {
+                    const int i = base + q * kNThreads + tid;
+                    cs[q] = i < n ? __ldcg(reinterpret_cast<const unsigned long long *>(list + i)) : 0ull;
+                }
+#pragma unroll
+                for (int q = 0; q < kScanUnroll; q++) {
+                    const uint64_t c = cs[q];
+                    if (base + q * kNThreads + tid >= n || c < kth) continue;
+                    const double e = exp((double) composite_value(c) - mx);
+                    part += e;
+                    const uint32_t b = mass_bucket(c, mxf);
+                    atomicAdd(&s_hmass[b], e);
+                    atomicAdd(&s_hcount[b], 1);
+                }
             }
             total = block_sum_double(part, s_red);
             __syncthreads();
