@@ -40,6 +40,7 @@ constexpr int kQueue = 256;         // pass 1's per-warp queue of a sparse round
 constexpr double kMargin = 1e-9;    // relative margin that decides a crossing without the exact path
 constexpr int kChunk = 256;         // exact path: values computed per step by the warp for lane 0's sums
 constexpr int kScanUnroll = 8;      // list entries requested together per thread by the list scans
+constexpr int kMergedScanMin = 16384;  // candidates from which one scan loads both crossings' buckets
 
 __device__ __forceinline__ uint32_t bucket_of(uint64_t c) { return (uint32_t) (c >> 32) >> kBucketShift; }
 
@@ -112,7 +113,7 @@ __global__ void __launch_bounds__(kNThreads, 1) nucleus_rows_kernel(const Nucleu
     __shared__ float s_redf[32];
     __shared__ int s_redi[32];
     __shared__ uint64_t s_red64[32];
-    __shared__ int s_n, s_lc;
+    __shared__ int s_n, s_lc, s_lc2;
     __shared__ double s_d0, s_d1;
     __shared__ int s_i0, s_i1;
 
@@ -392,7 +393,9 @@ __global__ void __launch_bounds__(kNThreads, 1) nucleus_rows_kernel(const Nucleu
                 if (in) atomicMax(&s_i0, b);
             }
             __syncthreads();
-            return s_i0;
+            const int r = s_i0;
+            __syncthreads();  // every thread holds the result before a following call resets s_i0
+            return r;
         };
         // Sorts bucket b's tokens of the list (descending) into s_list; returns their count, or -1 if too
         // many for shared memory.
@@ -432,13 +435,63 @@ __global__ void __launch_bounds__(kNThreads, 1) nucleus_rows_kernel(const Nucleu
             if (np2 > 1) bitonic_sort_desc(s_list, np2);
             return cnt;
         };
+        // One scan for both crossings: the tokens of mass bucket b1 into the first half of s_list and those
+        // of buckets lo..hi into the second, each half sorted; a count is -1 when its half overflows.
+        auto load_two = [&](int b1, int lo, int hi, uint64_t floor, int & c1, int & c2) {
+            constexpr int kHalf = kListMaxN / 2;
+            uint64_t * A = s_list;
+            uint64_t * B = s_list + kHalf;
+            if (tid == 0) s_lc = 0, s_lc2 = 0;
+            __syncthreads();
+            auto put = [&](bool in, uint64_t c, uint64_t * dst, int * counter) {
+                const unsigned m = __ballot_sync(0xffffffffu, in);
+                if (m) {
+                    int at = 0;
+                    if (lane == __ffs(m) - 1) at = atomicAdd(counter, __popc(m));
+                    at = __shfl_sync(0xffffffffu, at, __ffs(m) - 1);
+                    const int pos = at + __popc(m & ((1u << lane) - 1u));
+                    if (in && pos < kHalf) dst[pos] = c;
+                }
+            };
+            for (int base = 0; base < n; base += kNThreads * kScanUnroll) {  // uniform trip count
+                uint64_t cs[kScanUnroll];
+#pragma unroll
+                for (int q = 0; q < kScanUnroll; q++) {
+                    const int i = base + q * kNThreads + tid;
+                    cs[q] = i < n ? __ldcg(reinterpret_cast<const unsigned long long *>(list + i)) : 0ull;
+                }
+#pragma unroll
+                for (int q = 0; q < kScanUnroll; q++) {
+                    const int i = base + q * kNThreads + tid;
+                    const uint64_t c = cs[q];
+                    const int bk = (i < n && c >= floor) ? (int) mass_bucket(c, mxf) : -1;
+                    put(bk == b1, c, A, &s_lc);
+                    put(bk >= lo && bk <= hi, c, B, &s_lc2);
+                }
+            }
+            __syncthreads();
+            c1 = s_lc <= kHalf ? s_lc : -1;
+            c2 = s_lc2 <= kHalf ? s_lc2 : -1;
+            __syncthreads();  // every thread holds the counts before load_bucket may reset s_lc
+            for (int h = 0; h < 2; h++) {  // block-uniform
+                const int cnt = h == 0 ? c1 : c2;
+                if (cnt < 0) continue;
+                uint64_t * x = h == 0 ? A : B;
+                int np2 = 1;
+                while (np2 < cnt) np2 <<= 1;
+                for (int i = cnt + tid; i < np2; i += kNThreads) x[i] = 0ull;
+                __syncthreads();
+                if (np2 > 1) bitonic_sort_desc(x, np2);
+                __syncthreads();
+            }
+        };
         // In the sorted bucket list (cnt tokens, mass `above` before it): the first position whose running
         // mass reaches `target` (strict: exceeds it), with the running mass there (s_d0) and just before it
         // (s_d1); -1 when none in the list.
-        auto crossing_in_list = [&](int cnt, double above, double target, bool strict) {
+        auto crossing_in_list = [&](const uint64_t * L, int cnt, double above, double target, bool strict) {
             for (int base = 0; base < cnt; base += kNThreads) {  // uniform
                 const int i = base + tid;
-                const double e = i < cnt ? exp((double) composite_value(s_list[i]) - mx) : 0.0;
+                const double e = i < cnt ? exp((double) composite_value(L[i]) - mx) : 0.0;
                 const double incl = block_scan_incl(e, s_red) + above;
                 if (tid == 0) s_i1 = INT_MAX;
                 __syncthreads();
@@ -514,14 +567,30 @@ __global__ void __launch_bounds__(kNThreads, 1) nucleus_rows_kernel(const Nucleu
             int b1 = tp <= 1.0 ? crossing_bucket(tp * total, false) : -2;
             double T1 = total;  // pick()'s total (as running mass)
             int posk = n - 1;   // sorted position of the last kept token
+            // the draw's buckets are bounded before the cut is found: pick()'s total T1 lies in b1's share
+            // of the running mass, (above(b1), above(b1 - 1)], so the draw's target u * T1 lies between u
+            // times those two; for a long list one scan then loads b1 and that range (a short list is
+            // scanned twice more cheaply than the two bucket searches this costs)
+            int lo2 = -1, hi2 = -1, cnt2 = -1;
+            const uint64_t * L2 = s_list + kListMaxN / 2;
+            if (b1 >= 0 && n >= kMergedScanMin) {
+                const double a1 = s_hmass[b1], i1 = b1 > 0 ? s_hmass[b1 - 1] : total;
+                hi2 = crossing_bucket(u * a1, true);
+                lo2 = crossing_bucket(u * i1, true);
+            }
             if (b1 == -1) {
                 exact = true;
             } else if (b1 >= 0) {
-                const int cnt = load_bucket(b1, kth, true);
+                int cnt = -1;
+                if (lo2 >= 0 && hi2 >= lo2) load_two(b1, lo2, hi2, kth, cnt, cnt2);
+                if (cnt < 0) {
+                    cnt2 = -1;
+                    cnt = load_bucket(b1, kth, true);
+                }
                 if (cnt < 0) {
                     exact = true;
                 } else {
-                    const int j = crossing_in_list(cnt, s_hmass[b1], tp * total, false);
+                    const int j = crossing_in_list(s_list, cnt, s_hmass[b1], tp * total, false);
                     if (j < 0) {
                         exact = true;
                     } else {
@@ -544,23 +613,27 @@ __global__ void __launch_bounds__(kNThreads, 1) nucleus_rows_kernel(const Nucleu
                 if (b2 < 0) {
                     exact = true;
                 } else {
-                    const int cnt = load_bucket(b2, kth, true);
+                    // the range loaded with b1 when it holds b2, else b2 alone (over b1's list: the cut is done)
+                    const bool ranged = cnt2 >= 0 && b2 >= lo2 && b2 <= hi2;
+                    const int top = ranged ? hi2 : b2;
+                    const uint64_t * L = ranged ? L2 : s_list;
+                    const int cnt = ranged ? cnt2 : load_bucket(b2, kth, true);
                     if (cnt < 0) {
                         exact = true;
                     } else {
-                        const int j = crossing_in_list(cnt, s_hmass[b2], target, true);
+                        const int j = crossing_in_list(L, cnt, s_hmass[top], target, true);
                         if (j < 0) {
                             exact = true;
                         } else {
                             const double at = s_d0 / T1, before = s_d1 / T1;
                             if (!(at - u > kMargin && u - before > kMargin)) exact = true;
-                            const int pos = s_hcount[b2] + j;
+                            const int pos = s_hcount[top] + j;
                             if (pos >= keep - 1) {
                                 // no running sum of the first keep - 1 exceeds u: the last kept token
-                                if (posk == pos) chosen_id = (int32_t) composite_index(s_list[j]);
+                                if (posk == pos) chosen_id = (int32_t) composite_index(L[j]);
                                 else exact = true;  // the last kept token lies in another bucket
                             } else {
-                                chosen_id = (int32_t) composite_index(s_list[j]);
+                                chosen_id = (int32_t) composite_index(L[j]);
                             }
                         }
                     }
