@@ -196,11 +196,16 @@ __global__ void __launch_bounds__(kShardThreads) shard_select_kernel(const __gri
     // above it, so at least take of the row's elements do: the row's take best are all at or above it
     // (take <= k_cap <= 1024 <= 2 x threads). Elements whose restricted logit lies below `rb` cannot reach
     // it (raw_bound) and are not divided at all.
+    // (a radix select over the 32-bit keys: at least take of them reach its prefix, so the prefix's value
+    // is at or below the take-th largest)
     s_list[2 * tid] = (uint64_t) order_key(b0) << 32, s_list[2 * tid + 1] = (uint64_t) order_key(b1) << 32;
     if (tid == 0) s_n = 0;
     __syncthreads();
-    bitonic_sort_desc(s_list, 2 * kShardThreads);
-    const float fv = take > 0 ? key_value((uint32_t) (s_list[take - 1] >> 32)) : -kInf;  // the take-th largest value
+    float fv = -kInf;
+    if (take > 0) {  // block-uniform
+        radix_select(2 * kShardThreads, take, [&](int i) { return s_list[i]; }, sel, 4);
+        fv = key_value((uint32_t) (sel.prefix >> 32));
+    }
     uint64_t floor_key;
     float rb;
     if (take == 0) {
@@ -240,12 +245,29 @@ __global__ void __launch_bounds__(kShardThreads) shard_select_kernel(const __gri
     }
     __syncthreads();
     const bool fits = s_n <= kShardList;
-    if (take > 0 && fits) {
+    const uint64_t * sorted = s_list;  // the record's first entries, best first
+    int nsorted = take;                // how many of them are valid (the rest are written as 0)
+    if (take > 0 && fits && s_n <= kShardThreads) {
+        // one candidate per thread: each ranked against all (composites are distinct), the take best
+        // written to their places in the upper half of the list
+        const int n = s_n;
+        uint64_t * out = s_list + kShardList / 2;
+        if (tid < n) {
+            const uint64_t mine = s_list[tid];
+            int rank = 0;
+            for (int j = 0; j < n; j++) rank += s_list[j] > mine;
+            if (rank < take) out[rank] = mine;
+        }
+        __syncthreads();
+        sorted = out;
+        nsorted = n < take ? n : take;
+    } else if (take > 0 && fits) {
         const int n = s_n;
         const int np2 = next_pow2(n);
         for (int i = n + tid; i < np2; i += kShardThreads) s_list[i] = 0ull;
         __syncthreads();
         bitonic_sort_desc(s_list, np2);
+        nsorted = n < take ? n : take;
     } else if (take > 0) {
         // too many composites at the floor (a row of many equal logits): radix select, then the selected
         __syncthreads();
@@ -271,14 +293,14 @@ __global__ void __launch_bounds__(kShardThreads) shard_select_kernel(const __gri
     }
     const uint64_t word = ((uint64_t) __float_as_uint(mx) << 32) | (uint32_t) nan_scaled;
     if (sa.splits == 1) {
-        for (int i = tid; i < sa.k_cap; i += kShardThreads) rec[i] = i < take ? s_list[i] : 0ull;
+        for (int i = tid; i < sa.k_cap; i += kShardThreads) rec[i] = i < nsorted ? sorted[i] : 0ull;
         if (tid == 0) rec[sa.k_cap] = word;
         return;
     }
     // split rows: this part's record into the scratch; the row's last CTA to arrive merges the parts'
     // records (splits x k_cap composites, sorted) into the row's record and leaves the counter at 0
     uint64_t * part = sa.parts + ((int64_t) row * sa.splits + split) * (sa.k_cap + 1);
-    for (int i = tid; i < sa.k_cap; i += kShardThreads) part[i] = i < take ? s_list[i] : 0ull;
+    for (int i = tid; i < sa.k_cap; i += kShardThreads) part[i] = i < nsorted ? sorted[i] : 0ull;
     __syncthreads();
     if (tid == 0) {
         part[sa.k_cap] = word;
