@@ -1,8 +1,8 @@
-"""The filter kernel (ssb_filter.cu) against the oracle restatement on rows built to reach each of its
-paths: a first stage that makes a poor threshold (ascending rows: every warp's buffer fills and is cut
-again and again; descending rows: the first stage holds the best), the best tokens all penalized
-history tokens or banned, fewer kept candidates than k (the exact fallback), NaN and infinities,
-ragged tails behind aligned rows, one row split over many CTAs and whole rows per CTA. Token ids and
+"""The large-vocabulary path for top-k <= 128 on aligned rows (the top-k kernel, ssb_topk.cu) against
+the oracle restatement, on rows built to stress a streamed top-k: ascending rows (every block a new
+maximum, so a bound from part of the row is poor) and descending ones (the first blocks hold the
+best), the best tokens all penalized history tokens or banned, fewer allowed tokens than k, NaN and
+infinities, ragged tails behind aligned rows, one row split over many CTAs and whole rows per CTA. Token ids and
 statuses must equal the oracle's (a draw within 1e-12 of a cumulative-share boundary would be allowed
 and counted; none is expected)."""
 import numpy as np
@@ -39,7 +39,8 @@ def _check(engine, oracle, x, kw, hist=None, hlen=None, mask=None, kind=MASK_NON
 @pytest.mark.parametrize("kw", [dict(greedy=True), dict(temperature=0.8, top_k=40, top_p=0.95),
                                 dict(temperature=1.3, top_k=128, top_p=0.9)])
 def test_ascending_rows_cut_the_buffers(engine, oracle, bf16, rows, kw):
-    """Rising logits: the first stage holds the smallest, so the threshold passes nearly everything."""
+    """Rising logits: the first blocks hold the smallest, so any bound taken early lets nearly everything
+    through."""
     v = 151936
     rng = np.random.default_rng(rows * 7 + bf16)
     x = (np.linspace(-8.0, 8.0, v, dtype=np.float32)[None, :] + rng.standard_normal((rows, v)).astype(np.float32) * 0.01)
@@ -61,7 +62,7 @@ def test_descending_rows(engine, oracle, rows):
 @pytest.mark.parametrize("rows", [2, 40])
 def test_best_tokens_are_history_or_banned(engine, oracle, rows):
     """The 300 largest logits of each row are history tokens with a heavy penalty, or banned: the raw
-    candidates the filter keeps are nearly all dropped, and the history warps' values decide."""
+    block maxima overstate every restricted logit there, and the penalized values decide."""
     v = 151936
     rng = np.random.default_rng(11 + rows)
     x = rng.standard_normal((rows, v)).astype(np.float32)
@@ -79,7 +80,7 @@ def test_best_tokens_are_history_or_banned(engine, oracle, rows):
 
 
 def test_fewer_allowed_than_k(engine, oracle):
-    """An allow mask with 30 tokens and top-k 100: the candidates include -inf tokens, the exact path."""
+    """An allow mask with 30 tokens and top-k 100: the candidates include -inf tokens."""
     v, rows = 151936, 3
     rng = np.random.default_rng(5)
     x = rng.standard_normal((rows, v)).astype(np.float32)
@@ -133,7 +134,7 @@ def test_ragged_tails_on_aligned_rows(engine, oracle, vocab, bf16):
 
 @pytest.mark.parametrize("rows", [1, 3, 37, 300])
 def test_random_settings_large_vocab(engine, oracle, rows):
-    """Random settings over the filter kernel's range (top-k <= 128, aligned rows), penalties, masks."""
+    """Random settings over the top-k kernel's range (top-k <= 128, aligned rows), penalties, masks."""
     rng = np.random.default_rng(rows)
     v = int(rng.choice([9000, 65536, 151936]))
     x = (rng.standard_normal((rows, v)) * rng.choice([1.0, 3.0])).astype(np.float32)
