@@ -8,9 +8,10 @@
 //                        greedy row, with the token's GLOBAL index), sorted, into one record per row:
 //                        k_cap composites (0 = none) and a word (max bits << 32 | flags). Two passes over
 //                        the slice with eight loads in flight per thread and no atomics on the bulk: each
-//                        thread's two best composites give a floor (the k-th largest of them, below which
-//                        none of the k best lies); the composites at or above it (a few times k, at most
-//                        4096, else a radix select) are sorted.
+//                        thread's two best composites give a floor (the k-th largest of them, by a radix
+//                        select, below which none of the k best lies); the composites at or above it (a
+//                        few times k, at most 4096, else a radix select over the slice) are ranked by
+//                        counting (up to one per thread) or sorted.
 //   (the records of all ranks are all-gathered: one collective of rows * (k_cap + 1) * 8 bytes per rank)
 //   shard_merge_kernel   (every rank, identically) per row: the global maximum and flags give the row's
 //                        status exactly as the whole-row kernels decide it (restricted_status, then a NaN
